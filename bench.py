@@ -1,0 +1,298 @@
+"""Benchmark of the MoE block hot path (BASELINE metric: "MoE block us/token @decode M=1 (% HBM peak)").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE configs[1] at M=1, run as configs[4](a) runs it): a synthetic 16-layer stack of the bf16
+Ling-style MoE block (H=2048, 64 routed experts of I=1408 + a 2816-wide shared expert as two I-wide slots,
+softmax top-6 router, RMSNorm eps 1e-6, residual), random-init N(0, 0.02) weights generated on the device,
+one decode token. A "step" is one token through all 16 blocks, captured once in a CUDA graph and replayed:
+each block is ONE kernel (mv_block_decode). Weights touched per step (16 x ~139 MB) exceed the 126 MB L2,
+so no flush is needed between steps. value = device time per step / (16 blocks x N ranks), i.e. the
+whole-job time per block-token (lower is better; N > 1 runs independent replicas: decode does not shard).
+
+Keys beyond the base contract: roofline (HBM, measured copy peak), cpu_baseline (the oracle's torch-eager
+fp32 block on the host cores), e2e (the same metric through the public MoeBlock.decode API with the token
+copied host->device and the result device->host every step), gpu_launches, clocks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "ming-voice_b200"))
+
+import torch  # noqa: E402
+
+METRIC = "MoE block us/token @decode M=1 (% HBM peak); prefill tokens/s @1/2/4/8 GPU"
+UNIT = "us/token"
+LAYERS = 16
+H, I, E, TOPK, IS = 2048, 1408, 64, 6, 2816
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """dram read+write bytes per launch of the decode kernel from the committed ncu summary (or None)."""
+    import re
+    path = os.path.join(ROOT, "profiles", "moe_decode_kernel_block_m1.md")
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.e+]+)", open(path).read())
+        return float(m.group(1)) if m else None
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    def __init__(self, index):
+        self.index, self.samples, self.proc = index, [], None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 6:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=2)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[2 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def make_stack(device, seed=3):
+    """16 blocks of random N(0, 0.02) weights, generated on the device (seeded)."""
+    from mingmoe.block import MoeBlock
+    g = torch.Generator(device=device).manual_seed(seed)
+    blocks = []
+    for _ in range(LAYERS):
+        E1 = E + IS // I
+        w_gu = (torch.randn(E1, 2 * I, H, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        w_d = (torch.randn(E1, H, I, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        rw = (torch.randn(E, H, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        nw = torch.ones(H, dtype=torch.bfloat16, device=device)
+        blocks.append(MoeBlock(w_gu, w_d, rw, nw, top_k=TOPK, shared_ids=tuple(range(E, E1)), eps=1e-6))
+    return blocks
+
+
+def cpu_block_time_us(reps=5):
+    """The oracle's torch-eager fp32 block on the host cores: us per block-token at M=1."""
+    from oracle import moe_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    p = O.make_block_params(seed=3, dtype=torch.float32)
+    x = O.make_tokens(1, seed=3, dtype=torch.float32)
+    O.moe_block(x, p)  # warm-up
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.moe_block(x, p)
+        ts.append((time.perf_counter() - t0) * 1e6)
+    return statistics.median(ts), torch.get_num_threads(), f"1 token through 1 fp32 block, median of {reps}"
+
+
+def dist_setup(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return rank, world, local
+
+
+def run_reference(args):
+    rank, world, _ = dist_setup(args.gpus) if int(os.environ.get("WORLD_SIZE", "1")) > 1 else (0, 1, 0)
+    if rank != 0:
+        return
+    # the reference's CPU torch-eager path (restated in oracle/), all host threads, a bounded sample per step
+    from oracle import moe_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    p = O.make_block_params(seed=3, dtype=torch.float32)
+    x = O.make_tokens(1, seed=3, dtype=torch.float32)
+    for _ in range(args.warmup):
+        O.moe_block(x, p)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.moe_block(x, p)
+        ts.append((time.perf_counter() - t0) * 1e6)
+    v = sum(ts) / len(ts)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 2), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v / 1e3, 4), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode M=1, one MoE block (CPU torch-eager reference path, fp32)",
+                   "H": H, "I": I, "E": E, "top_k": TOPK, "shared_I": IS},
+        "cpu_baseline": {"value": round(v, 2), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": "1 token through 1 block per step (the 16-layer step scaled per block)"},
+        "e2e": {"value": round(v, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args):
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from oracle import moe_oracle as O
+    blocks = make_stack(dev)
+    x0 = O.make_tokens(1, seed=3).to(dev)
+    bufs = [torch.empty(1, H, dtype=torch.bfloat16, device=dev) for _ in range(LAYERS + 1)]
+    bufs[0].copy_(x0)
+    ids = torch.empty(1, TOPK + 2, dtype=torch.int32, device=dev)
+
+    def step():
+        for layer, blk in enumerate(blocks):
+            blk.decode(bufs[layer], out=bufs[layer + 1], ids=ids if layer == 0 else None)
+
+    step()  # creates the workspaces before capture
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        step()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    U = O.distinct_experts(ids.cpu()[:, :TOPK])
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    with ClockSampler(local) as clk:
+        barrier()
+        s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
+        s_ev.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e_ev.record()
+        barrier()
+        elapsed_ms = s_ev.elapsed_time(e_ev)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    elapsed_ms = t.item()
+    ms_per_step = elapsed_ms / args.steps
+    us_per_block = ms_per_step * 1e3 / LAYERS
+
+    # end to end through the public API: pinned host token in, result out, every step (eager calls)
+    h_in = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
+    h_in.copy_(x0.cpu())
+    h_out = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
+    for _ in range(args.warmup):
+        bufs[0].copy_(h_in, non_blocking=True)
+        step()
+        h_out.copy_(bufs[LAYERS], non_blocking=True)
+    barrier()
+    s2, e2 = torch.cuda.Event(True), torch.cuda.Event(True)
+    s2.record()
+    for _ in range(args.steps):
+        bufs[0].copy_(h_in, non_blocking=True)
+        step()
+        h_out.copy_(bufs[LAYERS], non_blocking=True)
+    e2.record()
+    barrier()
+    t2 = torch.tensor([s2.elapsed_time(e2)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
+    e2e_us = t2.item() / args.steps * 1e3 / LAYERS
+
+    peak, peak_kind = peaks()
+    byts = O.decode_bytes(U)  # algorithmic bytes of one block step (M=1)
+    achieved = byts / (us_per_block * 1e-6) / 1e9
+    out = None
+    if rank == 0:
+        cpu_v, cores, sample = cpu_block_time_us()
+        out = {
+            "metric": METRIC, "value": round(us_per_block / world, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights generated on the device; N(0,1) token)",
+            "config": {"workload": "decode M=1 through a 16-layer chain of MoE blocks (BASELINE configs[1] at M=1, "
+                                   "run as configs[4](a): one CUDA graph per step, one kernel per block)",
+                       "layers": LAYERS, "H": H, "I": I, "E": E, "top_k": TOPK, "shared_I": IS,
+                       "routed_experts_hit": U, "parallelism": f"replicas x{world}",
+                       "l2": "weights per step (16 x 139 MB) exceed L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
+                         "note": f"{byts / 1e6:.1f} MB algorithmic per block / (graph step time / 16); "
+                                 f"peak {peak_kind}"},
+            "cpu_baseline": {"value": round(cpu_v, 1), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(e2e_us / world, 3), "unit": UNIT, "h2d_bytes_per_step": H * 2,
+                    "d2h_bytes_per_step": H * 2},
+            "gpu_launches": LAYERS * args.steps,
+            "clocks": clk.summary(),
+        }
+    if world > 1:
+        torch.distributed.barrier()
+        del graph
+        torch.distributed.destroy_process_group()
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

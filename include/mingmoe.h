@@ -1,0 +1,176 @@
+/* mingmoe — C-ABI of the B200 (sm_100a) kernels for ming-voice's Ling-style MoE block.
+ *
+ * Every entry point takes raw device pointers, sizes, element strides, dtype codes and a cudaStream_t
+ * (passed as void*), enqueues its kernels on that stream without synchronising the host, and returns an
+ * int status (MV_OK = 0). On failure the message is available from mv_last_error() (thread-local). No entry
+ * point allocates device memory: callers pass a zero-initialised workspace where one is needed and query its
+ * size with the matching *_workspace_bytes function. A workspace may be reused by every call on one stream
+ * (the kernels leave it zeroed again), but two calls that can run at the same time need two workspaces.
+ *
+ * The Python modules fused_moe.py / fused_ops.py / fastlinear.py of the `ming-voice_b200` directory wrap
+ * these entry points behind the reference's own signatures; each declaration names the reference function
+ * it replaces (file:line in ming-voice).
+ */
+#ifndef MINGMOE_H
+#define MINGMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MV_API __attribute__((visibility("default")))
+#else
+#define MV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define MV_OK 0
+#define MV_ERR_INVALID 1     /* bad shape, size or argument */
+#define MV_ERR_ALIGN 2       /* pointer / stride alignment requirement not met */
+#define MV_ERR_CUDA 3        /* CUDA runtime error while launching */
+#define MV_ERR_UNSUPPORTED 4 /* dtype or option combination not implemented */
+#define MV_ERR_WORKSPACE 5   /* workspace missing or too small */
+
+/* ---- dtype codes ---- */
+#define MV_BF16 0
+#define MV_F16 1
+#define MV_F32 2
+#define MV_I8 3
+#define MV_I32 4
+#define MV_I64 5
+
+/* ---- router modes ---- */
+#define MV_ROUTE_SOFTMAX 0       /* softmax(logits [+ bias]) -> top-k -> renormalise (Ling v1 style) */
+#define MV_ROUTE_SIGMOID_GROUP 1 /* sigmoid + bias, group-limited top-k, renormalise, x scale (ming-voice) */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+MV_API int mv_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+MV_API const char* mv_last_error(void);
+
+/* Reads (synchronously, on `stream`) the device-side error word of a workspace: 0 = none, 1 = a bounded
+ * wait timed out, 2 = an expert id outside [0, E1) was skipped, 3 = a capacity was exceeded. `info` (may be
+ * NULL) receives where it was raised. With clear != 0 the word is reset. Host-synchronising; not for use
+ * inside stream capture. */
+MV_API int mv_workspace_status(void* workspace, int clear, unsigned int* code, unsigned int* info, void* stream);
+
+/* RMSNorm over the last dimension: replaces fused_ops.rms_norm (fused_ops.py:28-37, kernel :16-25).
+ * y[r] = cast(w * cast(x[r] / sqrt(mean(x[r]^2) + eps), x_dtype), y_dtype); fp32 statistics.
+ * x: rows x n (row stride x_stride elements, inner stride 1), dtype bf16/f16/f32; w: [n] bf16/f16/f32;
+ * y: rows x n contiguous. */
+MV_API int mv_rmsnorm(const void* x, int x_dtype, long long x_stride, const void* w, int w_dtype, void* y, int y_dtype,
+               int rows, int n, float eps, void* stream);
+
+/* Router for n_tokens tokens: replaces fused_ops.moe_route (fused_ops.py:96-103; kernels :40-93) in mode
+ * MV_ROUTE_SIGMOID_GROUP, and is the BASELINE softmax-top-k router in mode MV_ROUTE_SOFTMAX.
+ *  x        [n_tokens, H] bf16 (row stride x_stride), the normalised hidden states;
+ *  w        [E, H] router weight, dtype w_dtype in {f32 (the reference's w32 copy), bf16, i8};
+ *  w_scale  [E] per-row scale when w is i8 (dtype scale_dtype f32/bf16), else NULL;
+ *  bias     [E] f32 or NULL: added to the sigmoid scores (sigmoid mode) / to the logits (softmax mode);
+ *  logits_out [n_tokens, E] f32 (may be NULL);
+ *  ids_out  [n_tokens, top_k + n_shared] (i32 or i64); wts_out same shape f32: the top_k experts, largest
+ *           first, ties to the lower id, then the shared slots shared_id .. shared_id + n_shared - 1 with
+ *           weight 1.0 (fused_ops.py:89-93).
+ * Sigmoid mode: n_group groups, keep topk_group groups by their top-2 sum, weights renormalised with +1e-20
+ * and multiplied by `scale`. Softmax mode ignores n_group / topk_group / scale.
+ * Logits are accumulated in fp64 and rounded once to fp32 (order-independent selection).
+ * workspace: mv_route_workspace_bytes(n_tokens, E) bytes, zero-initialised. */
+MV_API int mv_route(int mode, const void* x, long long x_stride, const void* w, int w_dtype, const void* w_scale,
+             int scale_dtype, const float* bias, int n_tokens, int H, int E, int top_k, int n_group,
+             int topk_group, double scale, int n_shared, int shared_id, float* logits_out, void* ids_out,
+             int ids_dtype, float* wts_out, void* workspace, size_t workspace_bytes, void* stream);
+MV_API size_t mv_route_workspace_bytes(int n_tokens, int E);
+
+/* Symmetric per-row int8 quantisation: replaces fused_moe.quantize_rows_int8 (fused_moe.py:199-204).
+ * w: rows x K (row stride w_stride elements), bf16/f16/f32. q: rows x K int8 contiguous;
+ * scale: [rows], dtype scale_dtype (f32 = the reference's layout; bf16 = scale rounded to bf16 first and q
+ * computed against the rounded scale). amax = max|w| clamped to >= 1e-8, scale = amax / 127,
+ * q = round_half_even(w / scale) clamped to [-127, 127]; bit-exact with torch. */
+MV_API int mv_quantize_rows_int8(const void* w, int w_dtype, long long w_stride, long long rows, int K, int8_t* q,
+                          void* scale, int scale_dtype, void* stream);
+
+/* Dequantisation exactly as the int8 kernels perform it in registers: out = float(q) * float(scale[row]),
+ * one correctly rounded fp32 multiply (== torch q.float() * s.float()). Exported so the in-kernel
+ * dequantisation can be checked bit for bit. q: rows x K contiguous; out: rows x K f32. */
+MV_API int mv_dequant_rows_int8(const int8_t* q, const void* scale, int scale_dtype, long long rows, int K,
+                         float* out, void* stream);
+
+/* Stacked expert weights in the reference layout (engine.py:150-188, fused_moe.py:3-6):
+ * w_gu [E1, 2I, H] (gate rows [0, I), up rows [I, 2I)), w_d [E1, H, I]; inner stride 1; strides in elements.
+ * w_dtype MV_BF16 or MV_I8; int8 weights carry per-output-row scales s_gu [E1, 2I] and s_d [E1, H]
+ * (s_dtype MV_F32 or MV_BF16, inner stride 1). */
+typedef struct mv_moe_weights {
+  const void* w_gu;
+  const void* w_d;
+  const void* s_gu;
+  const void* s_d;
+  int w_dtype;
+  int s_dtype;
+  int E1;
+  int H;
+  int I;
+  int pad0;
+  long long gu_se, gu_sr; /* w_gu strides: expert, row */
+  long long d_se, d_sr;   /* w_d strides: expert, row */
+  long long sgu_se;       /* s_gu expert stride */
+  long long sd_se;        /* s_d expert stride */
+} mv_moe_weights;
+
+/* Decode MoE (M <= 16 tokens): replaces fused_moe.fused_moe_decode (fused_moe.py:67-83; kernels :14-61)
+ * and the M = 2..16 use of fused_moe_prefill (engine.py:381-382).
+ *   out[m] = cast_bf16( residual[m] + sum_k wts[m,k] * down_e(silu(gate_e(xn_m)) * up_e(xn_m)) ),  e = ids[m,k]
+ * x [M, H] bf16 (row stride x_stride). If norm_w (bf16 [H]) is non-NULL, xn = RMSNorm(x) with eps, computed
+ * as mv_rmsnorm does; otherwise xn = x. ids [M, NK] (i32 or i64, row stride NK), wts [M, NK] f32. ids outside
+ * [0, E1) are skipped and flagged in the workspace. residual [M, H] bf16 or NULL. out [M, H] bf16.
+ * Intermediates stay fp32 (no bf16 rounding of gate/up/act/per-expert outputs).
+ * One cooperative kernel (one CTA per SM): each CTA streams an equal share of the selected experts' gate/up
+ * rows, then (after one grid barrier) an equal share of output rows of their down projections.
+ * workspace: mv_moe_decode_workspace_bytes(M, NK, I, 0) bytes, zero-initialised (left zeroed).
+ * Requirements: M <= 16, NK <= 32, E1 <= 4096, H and I multiples of 8 (bf16) / 16 (i8), H <= 8192,
+ * 8 rows of w_d within 32 KB (I <= 2048 bf16 / 4096 i8), 16-byte aligned pointers and row strides. */
+MV_API int mv_moe_decode(const mv_moe_weights* w, const void* x, long long x_stride, const void* norm_w, float eps,
+                         const void* ids, int ids_dtype, const float* wts, int M, int NK, const void* residual,
+                         void* out, void* workspace, size_t workspace_bytes, void* stream);
+MV_API size_t mv_moe_decode_workspace_bytes(int M, int NK, int I, int E);
+
+/* One MoE block: RMSNorm -> router -> routed + shared experts -> residual. */
+typedef struct mv_block {
+  mv_moe_weights experts;   /* stacked routed experts and the shared-expert slot(s) */
+  const void* norm_w;       /* bf16 [H] post-attention RMSNorm weight (NULL: x is already normalised) */
+  const void* router_w;     /* [E, H] router weight, f32 / bf16 / i8 */
+  const void* router_scale; /* [E] row scales for an i8 router (f32 / bf16), else NULL */
+  const float* router_bias; /* [E] f32 or NULL (sigmoid mode: added to the scores; softmax: to the logits) */
+  float eps;
+  int router_dtype;
+  int router_scale_dtype;
+  int E;                    /* routed experts (ids 0..E-1 of the stacks) */
+  int top_k;
+  int route_mode;           /* MV_ROUTE_SOFTMAX or MV_ROUTE_SIGMOID_GROUP */
+  int n_group, topk_group;  /* sigmoid mode */
+  int n_shared;             /* shared-expert slots appended to every token with weight 1 */
+  int shared_id;            /* first shared slot (E in ming-voice's stacks) */
+  int residual_from_x;      /* 1: out = x + MoE(norm(x)) (the decoder layer's residual); 0: out = MoE(...) */
+  int pad0;
+  double route_scale;       /* sigmoid mode: routed_scaling_factor */
+} mv_block;
+
+/* Decode step of one block for M <= 16 tokens in ONE cooperative kernel: replaces the patched single-token
+ * MoE forward (engine.py:371-386: fused_ops.moe_route followed by fused_moe.fused_moe_decode), including the
+ * RMSNorm before it (engine.py:229) and the decoder layer's residual. x [M, H] bf16 contiguous, out [M, H] bf16.
+ * Optional router outputs (each may be NULL): logits_out [M, E] f32, ids_out [M, top_k + n_shared]
+ * (i32/i64), wts_out [M, top_k + n_shared] f32 -- the aux the reference block returns.
+ * workspace: mv_block_decode_workspace_bytes(M, top_k + n_shared, I, E) bytes, zero-initialised. */
+MV_API int mv_block_decode(const mv_block* b, const void* x, int M, void* out, float* logits_out, void* ids_out,
+                           int ids_dtype, float* wts_out, void* workspace, size_t workspace_bytes, void* stream);
+MV_API size_t mv_block_decode_workspace_bytes(int M, int n_experts_per_token, int I, int E);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINGMOE_H */
