@@ -101,12 +101,12 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-def make_stack(device, seed=3):
+def make_stack(device, layers, seed=3):
     """16 blocks of random N(0, 0.02) weights, generated on the device (seeded)."""
     from mingmoe.block import MoeBlock
     g = torch.Generator(device=device).manual_seed(seed)
     blocks = []
-    for _ in range(LAYERS):
+    for _ in range(layers):
         E1 = E + IS // I
         w_gu = (torch.randn(E1, 2 * I, H, generator=g, device=device) * 0.02).to(torch.bfloat16)
         w_d = (torch.randn(E1, H, I, generator=g, device=device) * 0.02).to(torch.bfloat16)
@@ -176,7 +176,8 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     from oracle import moe_oracle as O
-    blocks = make_stack(dev)
+    LAYERS = args.layers
+    blocks = make_stack(dev, LAYERS)
     x0 = O.make_tokens(1, seed=3).to(dev)
     bufs = [torch.empty(1, H, dtype=torch.bfloat16, device=dev) for _ in range(LAYERS + 1)]
     bufs[0].copy_(x0)
@@ -282,9 +283,10 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS, help="blocks in the chain (1 = the small profiling case)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
