@@ -169,6 +169,20 @@ MV_API int mv_block_decode(const mv_block* b, const void* x, int M, void* out, f
                            int ids_dtype, float* wts_out, void* workspace, size_t workspace_bytes, void* stream);
 MV_API size_t mv_block_decode_workspace_bytes(int M, int n_experts_per_token, int I, int E);
 
+/* mv_block_decode without a caller workspace: no counterpart in the reference (its Triton launches take
+ * torch-allocated buffers). For callers that cannot allocate device memory or keep a workspace -- a C/FFI
+ * host without a device allocator, or code that must not call cudaMalloc while a stream is captured.
+ * The scratch is a static 1 MiB device array per device; the first call on a device (with it current)
+ * looks its address up, so make that call before any stream capture. Calls whose scratch need
+ * (mv_block_decode_workspace_bytes) exceeds 1 MiB are rejected with MV_ERR_WORKSPACE. Each call clears the
+ * scratch's 256-byte header (barrier counters, error word) on `stream` before its launch.
+ * status_out (device or pinned host memory, 2 x u32, may be NULL) receives the call's device-side error
+ * code and location, as mv_workspace_status reports them. One scratch per device: calls that can run
+ * concurrently on one device race; keep them on one stream or order them with events. Allocates nothing. */
+MV_API int mv_block_decode_noalloc(const mv_block* b, const void* x, int M, void* out, float* logits_out,
+                                   void* ids_out, int ids_dtype, float* wts_out, unsigned int* status_out,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

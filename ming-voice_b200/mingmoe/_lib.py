@@ -59,6 +59,7 @@ _SIGS = {
     "mv_moe_decode_workspace_bytes": (SZ, [I32, I32, I32, I32]),
     "mv_block_decode": (I32, [C.POINTER(Block), P, I32, P, P, P, I32, P, P, SZ, P]),
     "mv_block_decode_workspace_bytes": (SZ, [I32, I32, I32, I32]),
+    "mv_block_decode_noalloc": (I32, [C.POINTER(Block), P, I32, P, P, P, I32, P, P, P]),
 }
 
 _lib = None
