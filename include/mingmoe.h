@@ -138,6 +138,30 @@ MV_API int mv_moe_decode(const mv_moe_weights* w, const void* x, long long x_str
                          void* out, void* workspace, size_t workspace_bytes, void* stream);
 MV_API size_t mv_moe_decode_workspace_bytes(int M, int NK, int I, int E);
 
+/* Sort of (token, slot) pairs by expert for the grouped GEMMs: replaces fused_moe._align_blocks
+ * (fused_moe.py:154-173), same outputs. ids [P] (i32/i64, the flattened [N, NK] expert ids). Each expert's
+ * pairs keep their index order (stable) and its run is padded to a multiple of BM rows.
+ *   sorted_out [nb_max * BM] i32: pair index, P for padding;  bexp_out [nb_max] i32: expert of each block,
+ *   -1 for unused blocks;  nb_used_out [1] i32: blocks in use;  nb_max = (P + E1 * (BM - 1) + BM - 1) / BM.
+ * ids outside [0, E1) are dropped and flagged in the workspace (>= 256 bytes, zero-initialised).
+ * Requirements: E1 <= 512, 1 <= BM <= 4096. */
+MV_API int mv_moe_align(const void* ids, int ids_dtype, int P, int E1, int BM, int* sorted_out, int* bexp_out,
+                        int* nb_used_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Prefill MoE for N tokens on the tensor cores (tcgen05): replaces fused_moe.fused_moe_prefill
+ * (fused_moe.py:176-196; kernels _moe_gu_grouped :93-121, _moe_down_grouped :125-148).
+ *   out[t] = bf16( residual[t] + sum_k wts[t,k] * down_e(bf16(silu(gate_e(x_t)) * up_e(x_t))) ), e = ids[t,k]
+ * x [N, H] bf16 (row stride x_stride), ids [N, NK] i32/i64, wts [N, NK] f32, residual [N, H] bf16 (row stride
+ * residual_stride) or NULL, out [N, H] bf16 contiguous. Gate/up accumulate in fp32; the activation is rounded
+ * to bf16 once (the tensor-core operand of the down projection); the per-pair outputs are weighted and summed
+ * in fp32 (reduction order not fixed). Weights bf16 (int8 prefill: see mv_moe_decode over chunks).
+ * workspace: mv_moe_prefill_workspace_bytes(N, NK, H, I, E1) bytes, 256-byte aligned, header zeroed.
+ * Requirements: H a multiple of 256, I a multiple of 128, E1 <= 512, 16-byte aligned pointers/strides. */
+MV_API int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids, int ids_dtype,
+                          const float* wts, int N, int NK, const void* residual, long long residual_stride, void* out,
+                          void* workspace, size_t workspace_bytes, void* stream);
+MV_API size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1);
+
 /* One MoE block: RMSNorm -> router -> routed + shared experts -> residual. */
 typedef struct mv_block {
   mv_moe_weights experts;   /* stacked routed experts and the shared-expert slot(s) */

@@ -1,0 +1,581 @@
+// Prefill MoE (any number of tokens) on the 5th-generation tensor cores.
+//
+// mv_moe_prefill replaces fused_moe.fused_moe_prefill (ming-voice fused_moe.py:176-196; kernels
+// _moe_gu_grouped :93-121, _moe_down_grouped :125-148) and mv_moe_align replaces _align_blocks (:154-173).
+//
+// Pipeline (five launches, no host synchronisation, capture-safe):
+//   1. align_kernel    stable counting sort of the (token, slot) pairs by expert, each expert's run padded to
+//                      128 rows; the same sorted_ids / bexp arrays the reference builds (pad id = P, unused
+//                      block = -1).
+//   2. gather_kernel   xs[r] = x[token of sorted pair r] (bf16, zero rows for pads) and y32 = residual (fp32).
+//   3. gemm_kernel<0>  per 128-pair block and 128-column slice of the intermediate dimension:
+//                      [gate | up] = xs_blk . W_gu[e]^T as ONE 128 x 256 tcgen05 tile (gate rows n0.., up rows
+//                      I+n0.. side by side in shared memory), epilogue a = bf16(silu(gate) * up).
+//   4. gemm_kernel<1>  per block and 256-column slice of H: o = a_blk . W_d[e]^T, epilogue
+//                      y32[token] += weight * o (fp32 vector reductions; pads skipped).
+//   5. finalize_kernel out = bf16(y32).
+// The GEMMs are persistent (one CTA per SM) and warp-specialised: warp 0 issues TMA loads into a 4-deep ring
+// of 48 KB stages (A 128x64, B 256x64 bf16, 128-byte swizzle), warp 1 issues tcgen05.mma (M=128, N=256,
+// K=16) into one of two TMEM accumulators (2 x 256 fp32 columns), warps 2-5 drain the other accumulator
+// (tcgen05.ld) while the next tile accumulates. Every wait is bounded (errors go to the workspace header).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace mv {
+namespace prefill {
+
+constexpr int kBM = 128;       // sorted pairs per block = MMA M
+constexpr int kBK = 64;        // K per stage: one 128-byte swizzle row of bf16
+constexpr int kGuHalf = 128;   // gate (and up) columns per gate/up tile: MMA N = 256
+constexpr int kDownN = 256;    // output columns per down tile: MMA N = 256
+constexpr int kStages = 4;
+constexpr int kAStageBytes = kBM * kBK * 2;   // 16 KB
+constexpr int kBStageBytes = 256 * kBK * 2;   // 32 KB
+constexpr int kStageBytes = kAStageBytes + kBStageBytes;
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr uint32_t kTmemCols = 512;
+constexpr int kAlignMaxE1 = 512;
+constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + 256;
+
+__device__ __forceinline__ int load_id(const void* ids, int ids_i64, int p) {
+  return ids_i64 ? static_cast<int>(static_cast<const long long*>(ids)[p]) : static_cast<const int*>(ids)[p];
+}
+
+// ------------------------------------------------------------------------------------------------ align
+
+// One CTA of 1024 threads. Stable: pairs of one expert keep their index order (the reference sorts with a
+// stable counting sort). Shared memory: cnt[E1], start[E1], run[E1], wcnt[32][E1] ints.
+__global__ void __launch_bounds__(1024) align_kernel(const void* __restrict__ ids, int ids_i64, int P, int E1, int BM,
+                                                     int nb_max, int* __restrict__ sorted, int* __restrict__ bexp,
+                                                     int* __restrict__ nb_used, WsHeader* ws) {
+  extern __shared__ int sm[];
+  int* cnt = sm;
+  int* start = cnt + E1;
+  int* run = start + E1;
+  int* wcnt = run + E1;
+  __shared__ int s_total;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E1; e += blockDim.x) {
+    cnt[e] = 0;
+    run[e] = 0;
+  }
+  for (int i = tid; i < 32 * E1; i += blockDim.x) wcnt[i] = 0;
+  __syncthreads();
+  for (int p = tid; p < P; p += blockDim.x) {
+    const int e = load_id(ids, ids_i64, p);
+    if (e >= 0 && e < E1)
+      atomicAdd(&cnt[e], 1);
+    else
+      raise_error(ws, kErrBadExpert, static_cast<unsigned int>(p));
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive scan of the padded run lengths
+    const int per = (E1 + 31) / 32;
+    const int lo = lane * per, hi = min(lo + per, E1);
+    int s = 0;
+    for (int e = lo; e < hi; ++e) s += (cnt[e] + BM - 1) / BM * BM;
+    int incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int ex = incl - s;
+    for (int e = lo; e < hi; ++e) {
+      start[e] = ex;
+      ex += (cnt[e] + BM - 1) / BM * BM;
+    }
+    if (lane == 31) s_total = incl;
+  }
+  __syncthreads();
+  const int total = s_total;
+  for (int r = tid; r < nb_max * BM; r += blockDim.x) sorted[r] = P;
+  for (int b = tid; b < nb_max; b += blockDim.x) {
+    int e = -1;
+    if (b * BM < total) {  // first expert whose padded run ends after row b*BM
+      int lo = 0, hi = E1 - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (start[mid] + (cnt[mid] + BM - 1) / BM * BM > b * BM)
+          hi = mid;
+        else
+          lo = mid + 1;
+      }
+      e = lo;
+    }
+    bexp[b] = e;
+  }
+  if (tid == 0) *nb_used = total / BM;
+  __syncthreads();
+  for (int base = 0; base < P; base += blockDim.x) {
+    const int p = base + tid;
+    int e = p < P ? load_id(ids, ids_i64, p) : -1;
+    const bool valid = e >= 0 && e < E1;
+    if (!valid) e = -1;
+    const unsigned int m = __match_any_sync(0xffffffffu, e);
+    const unsigned int before = m & ((1u << lane) - 1u);
+    const bool leader = before == 0u;
+    if (valid && leader) wcnt[warp * E1 + e] = __popc(m);
+    __syncthreads();
+    if (valid) {
+      int off = run[e] + __popc(before);
+      for (int w2 = 0; w2 < warp; ++w2) off += wcnt[w2 * E1 + e];
+      sorted[start[e] + off] = p;
+    }
+    __syncthreads();
+    if (valid && leader) {
+      atomicAdd(&run[e], __popc(m));
+      wcnt[warp * E1 + e] = 0;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ gather
+
+// One warp per row: rows [0, nb_used*128) of xs from the sorted pairs, then rows [0, N) of y32.
+__global__ void __launch_bounds__(256) gather_kernel(const uint16_t* __restrict__ x, long long x_stride,
+                                                     const int* __restrict__ sorted, const int* __restrict__ nb_used,
+                                                     int NK, int P, int H, uint16_t* __restrict__ xs,
+                                                     const uint16_t* __restrict__ residual, long long r_stride,
+                                                     float* __restrict__ y32, int N) {
+  const int lane = threadIdx.x & 31;
+  const long long rows_xs = static_cast<long long>(*nb_used) * kBM;
+  const long long total = rows_xs + N;
+  const int nv = H / 8;  // 16-byte vectors per row
+  for (long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < total;
+       row += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    if (row < rows_xs) {
+      const int p = sorted[row];
+      uint4* dst = reinterpret_cast<uint4*>(xs + row * H);
+      if (p < P) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<long long>(p / NK) * x_stride);
+        for (int v = lane; v < nv; v += 32) dst[v] = src[v];
+      } else {
+        for (int v = lane; v < nv; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      const long long t = row - rows_xs;
+      float4* dst = reinterpret_cast<float4*>(y32 + t * H);
+      if (residual != nullptr) {
+        const uint4* src = reinterpret_cast<const uint4*>(residual + t * r_stride);
+        for (int v = lane; v < nv; v += 32) {
+          const uint4 q = src[v];
+          dst[2 * v] = make_float4(bf16lo(q.x), bf16hi(q.x), bf16lo(q.y), bf16hi(q.y));
+          dst[2 * v + 1] = make_float4(bf16lo(q.z), bf16hi(q.z), bf16lo(q.w), bf16hi(q.w));
+        }
+      } else {
+        for (int v = lane; v < 2 * nv; v += 32) dst[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ y32, long long n4,
+                                                       uint16_t* __restrict__ out) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(y32)[i];
+    uint2 o;
+    o.x = static_cast<uint32_t>(f2bf(v.x)) | (static_cast<uint32_t>(f2bf(v.y)) << 16);
+    o.y = static_cast<uint32_t>(f2bf(v.z)) | (static_cast<uint32_t>(f2bf(v.w)) << 16);
+    reinterpret_cast<uint2*>(out)[i] = o;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ GEMMs
+
+struct GemmArgs {
+  const int* sorted;   // [nb_max * 128] pair ids (P = pad)
+  const int* bexp;     // [nb_max] expert per block
+  const int* nb_used;  // device scalar: blocks in use
+  int P, NK, H, I;
+  int n_tiles;         // N tiles per block
+  int k_steps;         // K / 64
+  uint16_t* a_out;     // gate/up: [rows, I] bf16
+  float* y32;          // down: [N, H] fp32 accumulator
+  const float* wts;    // down: [P] routing weights
+  WsHeader* ws;
+};
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
+
+// KIND 0: gate/up + SwiGLU, KIND 1: down + weighted scatter-add.
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                           const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stA = smem;
+  uint8_t* stB = smem + kStages * kAStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stB + kStages * kBStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* accf = empty + kStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* done = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 128);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const int total = *g.nb_used * g.n_tiles;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const int blk = tile / g.n_tiles, nt = tile - blk * g.n_tiles;
+        const int e = g.bexp[blk];
+        for (int k = 0; k < g.k_steps; ++k) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, g.ws, 0x500u + KIND)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          uint8_t* a = stA + stage * kAStageBytes;
+          uint8_t* b = stB + stage * kBStageBytes;
+          tc::tma_load_2d(a, &tmA, &full[stage], k * kBK, blk * kBM);
+          if (KIND == 0) {
+            tc::tma_load_3d(b, &tmB, &full[stage], k * kBK, nt * kGuHalf, e);
+            tc::tma_load_3d(b + kBStageBytes / 2, &tmB, &full[stage], k * kBK, g.I + nt * kGuHalf, e);
+          } else {
+            tc::tma_load_3d(b, &tmB, &full[stage], k * kBK, nt * kDownN, e);
+          }
+          ++issued;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // copies still in flight land before the CTA exits (immediate when the MMA warp consumed them)
+      for (int s = 0; s < kStages && s < issued; ++s) {
+        const int last_round = (issued - 1 - s) / kStages;
+        mbar_wait(&full[s], static_cast<uint32_t>(last_round & 1), g.ws, 0x510u + KIND);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(kBM, 256);
+      int stage = 0, j = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++j) {
+        const int buf = j & 1;
+        const uint32_t aph = static_cast<uint32_t>(j >> 1) & 1u;
+        if (!mbar_wait(&acce[buf], aph ^ 1u, g.ws, 0x520u + KIND)) break;
+        tc::fence_after_sync();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * 256);
+        for (int k = 0; k < g.k_steps; ++k) {
+          if (!mbar_wait(&full[stage], phase, g.ws, 0x530u + KIND)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint64_t ad = tc::sw128_desc(smem_u32(stA + stage * kAStageBytes));
+          const uint64_t bd = tc::sw128_desc(smem_u32(stB + stage * kBStageBytes));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc::mma_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (k | kk) != 0 ? 1u : 0u);
+          tc::mma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) tc::mma_commit(&accf[buf]);
+      }
+      // every issued MMA retires before the TMEM is released
+      tc::mma_commit(done);
+      mbar_wait(done, 0u, g.ws, 0x540u + KIND);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int g4 = warp & 3;  // the TMEM lane group this warp may access
+    const int row = g4 * 32 + lane;
+    int j = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++j) {
+      const int buf = j & 1;
+      const uint32_t aph = static_cast<uint32_t>(j >> 1) & 1u;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&accf[buf], aph, g.ws, 0x550u + KIND));
+      if (!ok) break;
+      tc::fence_after_sync();
+      const int blk = tile / g.n_tiles, nt = tile - blk * g.n_tiles;
+      const long long r = static_cast<long long>(blk) * kBM + row;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(g4 * 32) << 16) + static_cast<uint32_t>(buf * 256);
+      if (KIND == 0) {
+        uint4* dst = reinterpret_cast<uint4*>(g.a_out + r * g.I + nt * kGuHalf);
+#pragma unroll 1
+        for (int c = 0; c < kGuHalf / 32; ++c) {
+          uint32_t gr[32], ur[32];
+          tc::tmem_ld32(taddr + c * 32, gr);
+          tc::tmem_ld32(taddr + kGuHalf + c * 32, ur);
+          tc::tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float a0 = silu_mul(__uint_as_float(gr[2 * i]), __uint_as_float(ur[2 * i]));
+            const float a1 = silu_mul(__uint_as_float(gr[2 * i + 1]), __uint_as_float(ur[2 * i + 1]));
+            pk[i] = static_cast<uint32_t>(f2bf(a0)) | (static_cast<uint32_t>(f2bf(a1)) << 16);
+          }
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            dst[c * 4 + v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        }
+      } else {
+        const int p = g.sorted[r];
+        const bool live = p < g.P;
+        float w = 0.f;
+        float* dst = nullptr;
+        if (live) {
+          w = g.wts[p];
+          dst = g.y32 + static_cast<long long>(p / g.NK) * g.H + nt * kDownN;
+        }
+#pragma unroll 1
+        for (int c = 0; c < kDownN / 32; ++c) {
+          uint32_t v[32];
+          tc::tmem_ld32(taddr + c * 32, v);
+          tc::tmem_ld_wait();
+          if (live) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              red_add_v4_f32(dst + c * 32 + 4 * i, w * __uint_as_float(v[4 * i]), w * __uint_as_float(v[4 * i + 1]),
+                             w * __uint_as_float(v[4 * i + 2]), w * __uint_as_float(v[4 * i + 3]));
+          }
+        }
+      }
+      tc::fence_before_sync();
+      mbar_arrive(&acce[buf]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host
+
+struct Layout {
+  int P, nb_max;
+  long long rows;
+  size_t off_nb, off_sorted, off_bexp, off_xs, off_a, off_y32, total;
+};
+
+static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static Layout layout(int N, int NK, int H, int I, int E1) {
+  Layout L{};
+  L.P = N * NK;
+  L.nb_max = (L.P + E1 * (kBM - 1) + kBM - 1) / kBM;
+  L.rows = static_cast<long long>(L.nb_max) * kBM;
+  size_t o = kWsHeaderBytes;
+  L.off_nb = o;
+  o += 256;
+  L.off_sorted = o;
+  o = up(o + static_cast<size_t>(L.rows) * 4, 256);
+  L.off_bexp = o;
+  o = up(o + static_cast<size_t>(L.nb_max) * 4, 256);
+  L.off_xs = o;
+  o = up(o + static_cast<size_t>(L.rows) * H * 2, 256);
+  L.off_a = o;
+  o = up(o + static_cast<size_t>(L.rows) * I * 2, 256);
+  L.off_y32 = o;
+  o = up(o + static_cast<size_t>(N) * H * 4, 256);
+  L.total = o;
+  return L;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// bf16 tensor map, 128-byte swizzle, box inner 64 elements. dims/strides innermost first; strides in bytes.
+static int make_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                     const uint32_t* box, const char* what) {
+  auto enc = encode_fn();
+  if (enc == nullptr) return fail(MV_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
+                         reinterpret_cast<const cuuint64_t*>(dims), reinterpret_cast<const cuuint64_t*>(strides),
+                         reinterpret_cast<const cuuint32_t*>(box), estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MV_ERR_INVALID, "tensor map for %s rejected (CUresult %d)", what, static_cast<int>(r));
+  return MV_OK;
+}
+
+static int launch_align(const void* ids, int ids_dtype, int P, int E1, int BM, int nb_max, int* sorted, int* bexp,
+                        int* nb_used, WsHeader* ws, cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(35) * E1 * sizeof(int);
+  cudaError_t e = cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(align)");
+  align_kernel<<<1, 1024, smem, st>>>(ids, ids_dtype == MV_I64, P, E1, BM, nb_max, sorted, bexp, nb_used, ws);
+  return cuda_status(cudaGetLastError(), "align launch");
+}
+
+}  // namespace prefill
+}  // namespace mv
+
+using namespace mv;
+using namespace mv::prefill;
+
+extern "C" int mv_moe_align(const void* ids, int ids_dtype, int P, int E1, int BM, int* sorted_out, int* bexp_out,
+                            int* nb_used_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (ids_dtype != MV_I32 && ids_dtype != MV_I64) return fail(MV_ERR_INVALID, "mv_moe_align: ids must be i32 or i64");
+  if (P < 0 || E1 < 1 || E1 > kAlignMaxE1 || BM < 1 || BM > 4096)
+    return fail(MV_ERR_INVALID, "mv_moe_align: bad P=%d / E1=%d (<= %d) / BM=%d", P, E1, kAlignMaxE1, BM);
+  if ((P > 0 && ids == nullptr) || sorted_out == nullptr || bexp_out == nullptr || nb_used_out == nullptr)
+    return fail(MV_ERR_INVALID, "mv_moe_align: null pointer");
+  if (workspace == nullptr || workspace_bytes < kWsHeaderBytes)
+    return fail(MV_ERR_WORKSPACE, "mv_moe_align: workspace of %zu bytes needed", kWsHeaderBytes);
+  const long long nb_max = (static_cast<long long>(P) + static_cast<long long>(E1) * (BM - 1) + BM - 1) / BM;
+  if (nb_max * BM > 0x7fffffffLL) return fail(MV_ERR_INVALID, "mv_moe_align: too many pairs");
+  return launch_align(ids, ids_dtype, P, E1, BM, static_cast<int>(nb_max), sorted_out, bexp_out, nb_used_out,
+                      static_cast<WsHeader*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1) {
+  if (N < 0 || NK < 1 || H < 1 || I < 1 || E1 < 1) return 0;
+  return layout(N, NK, H, I, E1).total;
+}
+
+extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids,
+                              int ids_dtype, const float* wts, int N, int NK, const void* residual,
+                              long long residual_stride, void* out, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  if (w == nullptr || (N > 0 && (x == nullptr || ids == nullptr || wts == nullptr || out == nullptr)))
+    return fail(MV_ERR_INVALID, "mv_moe_prefill: null pointer argument");
+  if (ids_dtype != MV_I32 && ids_dtype != MV_I64) return fail(MV_ERR_INVALID, "mv_moe_prefill: ids must be i32 or i64");
+  if (w->w_dtype != MV_BF16) return fail(MV_ERR_UNSUPPORTED, "mv_moe_prefill: tensor-core path takes bf16 weights");
+  const int H = w->H, I = w->I, E1 = w->E1;
+  if (N < 0 || NK < 1 || NK > 64) return fail(MV_ERR_INVALID, "mv_moe_prefill: bad N=%d / NK=%d", N, NK);
+  if (H % kDownN != 0 || I % kGuHalf != 0 || H > 65536 || I > 65536)
+    return fail(MV_ERR_INVALID, "mv_moe_prefill: H=%d must be a multiple of %d and I=%d of %d", H, kDownN, I, kGuHalf);
+  if (E1 < 1 || E1 > kAlignMaxE1) return fail(MV_ERR_INVALID, "mv_moe_prefill: E1=%d outside [1, %d]", E1, kAlignMaxE1);
+  if (static_cast<long long>(N) * NK > 0x7fffffffLL / 2) return fail(MV_ERR_INVALID, "mv_moe_prefill: too many pairs");
+  if (N == 0) return MV_OK;
+  if (!aligned16(w->w_gu) || !aligned16(w->w_d) || !aligned16(x) || !aligned16(out) ||
+      (residual != nullptr && (!aligned16(residual) || (residual_stride * 2) % 16)) || (x_stride * 2) % 16 ||
+      (w->gu_sr * 2) % 16 || (w->gu_se * 2) % 16 || (w->d_sr * 2) % 16 || (w->d_se * 2) % 16)
+    return fail(MV_ERR_ALIGN, "mv_moe_prefill: pointers and row strides must be 16-byte aligned");
+  if (x_stride < H || (residual != nullptr && residual_stride < H))
+    return fail(MV_ERR_INVALID, "mv_moe_prefill: row stride shorter than H");
+  const Layout L = layout(N, NK, H, I, E1);
+  if (workspace == nullptr || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(MV_ERR_WORKSPACE, "mv_moe_prefill: 256-byte aligned workspace of %zu bytes needed", L.total);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  WsHeader* hdr = reinterpret_cast<WsHeader*>(ws);
+  int* nb_used = reinterpret_cast<int*>(ws + L.off_nb);
+  int* sorted = reinterpret_cast<int*>(ws + L.off_sorted);
+  int* bexp = reinterpret_cast<int*>(ws + L.off_bexp);
+  uint16_t* xs = reinterpret_cast<uint16_t*>(ws + L.off_xs);
+  uint16_t* abuf = reinterpret_cast<uint16_t*>(ws + L.off_a);
+  float* y32 = reinterpret_cast<float*>(ws + L.off_y32);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  CUtensorMap tm_xs, tm_wgu, tm_a, tm_wd;
+  int rc;
+  {
+    const uint64_t d[2] = {static_cast<uint64_t>(H), static_cast<uint64_t>(L.rows)};
+    const uint64_t s[1] = {static_cast<uint64_t>(H) * 2};
+    const uint32_t b[2] = {kBK, kBM};
+    if ((rc = make_tmap(&tm_xs, xs, 2, d, s, b, "xs")) != MV_OK) return rc;
+  }
+  {
+    const uint64_t d[3] = {static_cast<uint64_t>(H), static_cast<uint64_t>(2 * I), static_cast<uint64_t>(E1)};
+    const uint64_t s[2] = {static_cast<uint64_t>(w->gu_sr) * 2, static_cast<uint64_t>(w->gu_se) * 2};
+    const uint32_t b[3] = {kBK, kGuHalf, 1};
+    if ((rc = make_tmap(&tm_wgu, w->w_gu, 3, d, s, b, "w_gu")) != MV_OK) return rc;
+  }
+  {
+    const uint64_t d[2] = {static_cast<uint64_t>(I), static_cast<uint64_t>(L.rows)};
+    const uint64_t s[1] = {static_cast<uint64_t>(I) * 2};
+    const uint32_t b[2] = {kBK, kBM};
+    if ((rc = make_tmap(&tm_a, abuf, 2, d, s, b, "a")) != MV_OK) return rc;
+  }
+  {
+    const uint64_t d[3] = {static_cast<uint64_t>(I), static_cast<uint64_t>(H), static_cast<uint64_t>(E1)};
+    const uint64_t s[2] = {static_cast<uint64_t>(w->d_sr) * 2, static_cast<uint64_t>(w->d_se) * 2};
+    const uint32_t b[3] = {kBK, kDownN, 1};
+    if ((rc = make_tmap(&tm_wd, w->w_d, 3, d, s, b, "w_d")) != MV_OK) return rc;
+  }
+
+  if ((rc = launch_align(ids, ids_dtype, L.P, E1, kBM, L.nb_max, sorted, bexp, nb_used, hdr, st)) != MV_OK) return rc;
+  const int G = num_sms();
+  gather_kernel<<<G * 4, 256, 0, st>>>(static_cast<const uint16_t*>(x), x_stride, sorted, nb_used, NK, L.P, H, xs,
+                                       static_cast<const uint16_t*>(residual), residual_stride, y32, N);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "gather launch");
+
+  GemmArgs ga{};
+  ga.sorted = sorted;
+  ga.bexp = bexp;
+  ga.nb_used = nb_used;
+  ga.P = L.P;
+  ga.NK = NK;
+  ga.H = H;
+  ga.I = I;
+  ga.a_out = abuf;
+  ga.y32 = y32;
+  ga.wts = wts;
+  ga.ws = hdr;
+  e = cudaFuncSetAttribute(gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kGemmSmem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kGemmSmem));
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm)");
+  ga.n_tiles = I / kGuHalf;
+  ga.k_steps = H / kBK;
+  gemm_kernel<0><<<G, kThreads, kGemmSmem, st>>>(tm_xs, tm_wgu, ga);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "gate/up GEMM launch");
+  ga.n_tiles = H / kDownN;
+  ga.k_steps = I / kBK;
+  gemm_kernel<1><<<G, kThreads, kGemmSmem, st>>>(tm_a, tm_wd, ga);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "down GEMM launch");
+  const long long n4 = static_cast<long long>(N) * H / 4;
+  long long blocks = (n4 + 255) / 256;
+  if (blocks > G * 8) blocks = G * 8;
+  finalize_kernel<<<static_cast<unsigned int>(blocks), 256, 0, st>>>(y32, n4, static_cast<uint16_t*>(out));
+  return cuda_status(cudaGetLastError(), "finalize launch");
+}
