@@ -46,6 +46,15 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def peaks_tensor():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def ncu_traffic():
     """dram read+write bytes per launch of the decode kernel from the committed ncu summary (or None)."""
     import re
@@ -171,6 +180,58 @@ def run_reference(args):
     }), flush=True)
 
 
+def prefill_lines(dev, steps, warmup):
+    """BASELINE C4 on one block: 2043 packed tokens (37/211/512/1283), Zipf router bias, seed 2; one CUDA
+    graph per pass (RMSNorm, router, expert sort, gather, two tcgen05 grouped GEMMs, finalize)."""
+    from mingmoe.block import MoeBlock
+    from oracle import moe_oracle as O
+    p = O.make_block_params(seed=2, dtype=torch.bfloat16)
+    blk = MoeBlock.from_params(p, device=dev, router_bias=O.zipf_bias(E))
+    del p
+    N = sum(O.PREFILL_LENS)
+    x = O.make_tokens(N, seed=2).to(dev)
+    out = {}
+    blk.prefill(x)  # workspaces exist before capture
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        blk.prefill(x)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            y = blk.prefill(x)
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
+    s_ev.record()
+    for _ in range(steps):
+        graph.replay()
+    e_ev.record()
+    torch.cuda.synchronize()
+    us = s_ev.elapsed_time(e_ev) / steps * 1e3
+    # end to end through MoeBlock.prefill: pinned host tokens in, result out, every pass
+    h_in = x.cpu().pin_memory()
+    h_out = torch.empty_like(h_in).pin_memory()
+    for _ in range(warmup):
+        h_out.copy_(blk.prefill(h_in.to(dev, non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(True), torch.cuda.Event(True)
+    s2.record()
+    for _ in range(steps):
+        h_out.copy_(blk.prefill(h_in.to(dev, non_blocking=True)), non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    us_e2e = s2.elapsed_time(e2) / steps * 1e3
+    flops = O.prefill_flops(N)
+    del graph, y
+    return {"tokens": N, "us_per_pass": round(us, 1), "tokens_per_s": round(N / us * 1e6, 0),
+            "tflops": round(flops / us / 1e6, 1), "e2e_tokens_per_s": round(N / us_e2e * 1e6, 0),
+            "launches_per_pass": 10, "flops_per_pass": flops}
+
+
 def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -246,6 +307,7 @@ def run_ours(args):
         torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
     e2e_us = t2.item() / args.steps * 1e3 / LAYERS
 
+    pre = prefill_lines(dev, max(3, min(args.steps, 50)), args.warmup) if not args.no_prefill else None
     peak, peak_kind = peaks()
     byts = O.decode_bytes(U)  # algorithmic bytes of one block step (M=1)
     achieved = byts / (us_per_block * 1e-6) / 1e9
@@ -272,6 +334,12 @@ def run_ours(args):
             "gpu_launches": LAYERS * args.steps,
             "clocks": clk.summary(),
         }
+        if pre is not None:
+            tf_peak, tf_kind = peaks_tensor()
+            out["prefill"] = {"metric": "prefill tokens/s (BASELINE configs[3], 1 GPU, one block)", **pre,
+                              "roofline": {"bound": "tensor", "achieved": pre["tflops"], "peak": tf_peak,
+                                           "unit": "TFLOP/s", "frac": round(pre["tflops"] / tf_peak, 4),
+                                           "note": f"algorithmic FLOPs / graph pass time; peak {tf_kind}"}}
     if world > 1:
         torch.distributed.barrier()
         del graph
@@ -287,11 +355,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="blocks in the chain (1 = the small profiling case)")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) measurement")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the prefill measurement (the profiling case for the grouped GEMMs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.prefill_only:
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+        print(json.dumps(prefill_lines(dev, args.steps, args.warmup)), flush=True)
     else:
         run_ours(args)
 

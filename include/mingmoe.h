@@ -143,10 +143,11 @@ MV_API size_t mv_moe_decode_workspace_bytes(int M, int NK, int I, int E);
  * pairs keep their index order (stable) and its run is padded to a multiple of BM rows.
  *   sorted_out [nb_max * BM] i32: pair index, P for padding;  bexp_out [nb_max] i32: expert of each block,
  *   -1 for unused blocks;  nb_used_out [1] i32: blocks in use;  nb_max = (P + E1 * (BM - 1) + BM - 1) / BM.
- * ids outside [0, E1) are dropped and flagged in the workspace (>= 256 bytes, zero-initialised).
- * Requirements: E1 <= 512, 1 <= BM <= 4096. */
+ * ids outside [0, E1) are dropped and flagged in the workspace (mv_moe_align_workspace_bytes(P, E1) bytes,
+ * header zero-initialised). Requirements: E1 <= 512, 1 <= BM <= 4096. */
 MV_API int mv_moe_align(const void* ids, int ids_dtype, int P, int E1, int BM, int* sorted_out, int* bexp_out,
                         int* nb_used_out, void* workspace, size_t workspace_bytes, void* stream);
+MV_API size_t mv_moe_align_workspace_bytes(int P, int E1);
 
 /* Prefill MoE for N tokens on the tensor cores (tcgen05): replaces fused_moe.fused_moe_prefill
  * (fused_moe.py:176-196; kernels _moe_gu_grouped :93-121, _moe_down_grouped :125-148).

@@ -3,10 +3,10 @@
 // mv_moe_prefill replaces fused_moe.fused_moe_prefill (ming-voice fused_moe.py:176-196; kernels
 // _moe_gu_grouped :93-121, _moe_down_grouped :125-148) and mv_moe_align replaces _align_blocks (:154-173).
 //
-// Pipeline (five launches, no host synchronisation, capture-safe):
-//   1. align_kernel    stable counting sort of the (token, slot) pairs by expert, each expert's run padded to
-//                      128 rows; the same sorted_ids / bexp arrays the reference builds (pad id = P, unused
-//                      block = -1).
+// Pipeline (seven launches, no host synchronisation, capture-safe):
+//   1. align_*_kernel  stable counting sort of the (token, slot) pairs by expert, each expert's run padded to
+//                      128 rows (three launches); the same sorted_ids / bexp arrays the reference builds
+//                      (pad id = P, unused block = -1).
 //   2. gather_kernel   xs[r] = x[token of sorted pair r] (bf16, zero rows for pads) and y32 = residual (fp32).
 //   3. gemm_kernel<0>  per 128-pair block and 128-column slice of the intermediate dimension:
 //                      [gate | up] = xs_blk . W_gu[e]^T as ONE 128 x 256 tcgen05 tile (gate rows n0.., up rows
@@ -48,30 +48,56 @@ __device__ __forceinline__ int load_id(const void* ids, int ids_i64, int p) {
 
 // ------------------------------------------------------------------------------------------------ align
 
-// One CTA of 1024 threads. Stable: pairs of one expert keep their index order (the reference sorts with a
-// stable counting sort). Shared memory: cnt[E1], start[E1], run[E1], wcnt[32][E1] ints.
-__global__ void __launch_bounds__(1024) align_kernel(const void* __restrict__ ids, int ids_i64, int P, int E1, int BM,
-                                                     int nb_max, int* __restrict__ sorted, int* __restrict__ bexp,
-                                                     int* __restrict__ nb_used, WsHeader* ws) {
-  extern __shared__ int sm[];
-  int* cnt = sm;
-  int* start = cnt + E1;
-  int* run = start + E1;
-  int* wcnt = run + E1;
-  __shared__ int s_total;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int e = tid; e < E1; e += blockDim.x) {
-    cnt[e] = 0;
-    run[e] = 0;
-  }
-  for (int i = tid; i < 32 * E1; i += blockDim.x) wcnt[i] = 0;
+// Three launches over chunks of kChunk pairs. Stable: pairs of one expert keep their index order (the
+// reference's counting sort), because chunk c's pairs follow chunk c-1's and, inside a chunk, warp w's
+// follow warp w-1's and lane order is kept within a warp.
+//   align_count_kernel   (one CTA per chunk) per-chunk histogram hist[c][e]
+//   align_scan_kernel    (one CTA) hist -> exclusive prefix over chunks, padded run starts, bexp, nb_used,
+//                        padding ids (P) for the rows no pair lands on
+//   align_scatter_kernel (one CTA per chunk) sorted[start[e] + hist[c][e] + rank] = pair
+constexpr int kChunk = 1024;
+
+static size_t align_scratch_bytes(int P, int E1) {
+  const size_t nch = static_cast<size_t>(P + kChunk - 1) / kChunk;
+  return (nch * E1 + E1) * sizeof(int);
+}
+
+
+__global__ void __launch_bounds__(kChunk) align_count_kernel(const void* __restrict__ ids, int ids_i64, int P, int E1,
+                                                             int* __restrict__ hist, WsHeader* ws) {
+  extern __shared__ int sh[];
+  for (int e = threadIdx.x; e < E1; e += blockDim.x) sh[e] = 0;
   __syncthreads();
-  for (int p = tid; p < P; p += blockDim.x) {
+  const int p = blockIdx.x * kChunk + threadIdx.x;
+  if (p < P) {
     const int e = load_id(ids, ids_i64, p);
     if (e >= 0 && e < E1)
-      atomicAdd(&cnt[e], 1);
+      atomicAdd(&sh[e], 1);
     else
       raise_error(ws, kErrBadExpert, static_cast<unsigned int>(p));
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E1; e += blockDim.x) hist[static_cast<long long>(blockIdx.x) * E1 + e] = sh[e];
+}
+
+__global__ void __launch_bounds__(1024) align_scan_kernel(int P, int E1, int BM, int nb_max, int nch,
+                                                          int* __restrict__ hist, int* __restrict__ start_g,
+                                                          int* __restrict__ sorted, int* __restrict__ bexp,
+                                                          int* __restrict__ nb_used) {
+  extern __shared__ int sh[];
+  int* cnt = sh;
+  int* start = sh + E1;
+  __shared__ int s_total;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E1; e += blockDim.x) {  // exclusive prefix over chunks, per expert
+    int acc = 0;
+    for (int c = 0; c < nch; ++c) {
+      const long long i = static_cast<long long>(c) * E1 + e;
+      const int v = hist[i];
+      hist[i] = acc;
+      acc += v;
+    }
+    cnt[e] = acc;
   }
   __syncthreads();
   if (warp == 0) {  // exclusive scan of the padded run lengths
@@ -94,7 +120,12 @@ __global__ void __launch_bounds__(1024) align_kernel(const void* __restrict__ id
   }
   __syncthreads();
   const int total = s_total;
-  for (int r = tid; r < nb_max * BM; r += blockDim.x) sorted[r] = P;
+  for (int e = tid; e < E1; e += blockDim.x) {
+    start_g[e] = start[e];
+    const int pad_end = start[e] + (cnt[e] + BM - 1) / BM * BM;
+    for (int r = start[e] + cnt[e]; r < pad_end; ++r) sorted[r] = P;
+  }
+  for (int r = total + tid; r < nb_max * BM; r += blockDim.x) sorted[r] = P;
   for (int b = tid; b < nb_max; b += blockDim.x) {
     int e = -1;
     if (b * BM < total) {  // first expert whose padded run ends after row b*BM
@@ -111,28 +142,28 @@ __global__ void __launch_bounds__(1024) align_kernel(const void* __restrict__ id
     bexp[b] = e;
   }
   if (tid == 0) *nb_used = total / BM;
+}
+
+__global__ void __launch_bounds__(kChunk) align_scatter_kernel(const void* __restrict__ ids, int ids_i64, int P,
+                                                               int E1, const int* __restrict__ hist,
+                                                               const int* __restrict__ start_g,
+                                                               int* __restrict__ sorted) {
+  extern __shared__ int wcnt[];  // [32][E1]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int p = blockIdx.x * kChunk + tid;
+  int e = p < P ? load_id(ids, ids_i64, p) : -1;
+  const bool valid = e >= 0 && e < E1;
+  if (!valid) e = -1;
+  const unsigned int m = __match_any_sync(0xffffffffu, e);
+  const unsigned int before = m & ((1u << lane) - 1u);
+  for (int i = tid; i < 32 * E1; i += blockDim.x) wcnt[i] = 0;
   __syncthreads();
-  for (int base = 0; base < P; base += blockDim.x) {
-    const int p = base + tid;
-    int e = p < P ? load_id(ids, ids_i64, p) : -1;
-    const bool valid = e >= 0 && e < E1;
-    if (!valid) e = -1;
-    const unsigned int m = __match_any_sync(0xffffffffu, e);
-    const unsigned int before = m & ((1u << lane) - 1u);
-    const bool leader = before == 0u;
-    if (valid && leader) wcnt[warp * E1 + e] = __popc(m);
-    __syncthreads();
-    if (valid) {
-      int off = run[e] + __popc(before);
-      for (int w2 = 0; w2 < warp; ++w2) off += wcnt[w2 * E1 + e];
-      sorted[start[e] + off] = p;
-    }
-    __syncthreads();
-    if (valid && leader) {
-      atomicAdd(&run[e], __popc(m));
-      wcnt[warp * E1 + e] = 0;
-    }
-    __syncthreads();
+  if (valid && before == 0u) wcnt[warp * E1 + e] = __popc(m);
+  __syncthreads();
+  if (valid) {
+    int off = start_g[e] + hist[static_cast<long long>(blockIdx.x) * E1 + e] + __popc(before);
+    for (int w2 = 0; w2 < warp; ++w2) off += wcnt[w2 * E1 + e];
+    sorted[off] = p;
   }
 }
 
@@ -392,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 struct Layout {
   int P, nb_max;
   long long rows;
-  size_t off_nb, off_sorted, off_bexp, off_xs, off_a, off_y32, total;
+  size_t off_nb, off_align, off_sorted, off_bexp, off_xs, off_a, off_y32, total;
 };
 
 static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -405,6 +436,8 @@ static Layout layout(int N, int NK, int H, int I, int E1) {
   size_t o = kWsHeaderBytes;
   L.off_nb = o;
   o += 256;
+  L.off_align = o;
+  o = up(o + align_scratch_bytes(L.P, E1), 256);
   L.off_sorted = o;
   o = up(o + static_cast<size_t>(L.rows) * 4, 256);
   L.off_bexp = o;
@@ -446,13 +479,27 @@ static int make_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t*
   return MV_OK;
 }
 
+// scratch: align_scratch_bytes(P, E1) bytes (hist [nch][E1], start [E1])
 static int launch_align(const void* ids, int ids_dtype, int P, int E1, int BM, int nb_max, int* sorted, int* bexp,
-                        int* nb_used, WsHeader* ws, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(35) * E1 * sizeof(int);
-  cudaError_t e = cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+                        int* nb_used, int* scratch, WsHeader* ws, cudaStream_t st) {
+  const int nch = (P + kChunk - 1) / kChunk;
+  int* hist = scratch;
+  int* start = scratch + static_cast<size_t>(nch) * E1;
+  const size_t sm_scatter = static_cast<size_t>(32) * E1 * sizeof(int);
+  cudaError_t e = cudaFuncSetAttribute(align_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(sm_scatter));
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(align)");
-  align_kernel<<<1, 1024, smem, st>>>(ids, ids_dtype == MV_I64, P, E1, BM, nb_max, sorted, bexp, nb_used, ws);
-  return cuda_status(cudaGetLastError(), "align launch");
+  if (nch > 0) {
+    align_count_kernel<<<nch, kChunk, E1 * sizeof(int), st>>>(ids, ids_dtype == MV_I64, P, E1, hist, ws);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "align count launch");
+  }
+  align_scan_kernel<<<1, 1024, 2 * E1 * sizeof(int), st>>>(P, E1, BM, nb_max, nch, hist, start, sorted, bexp, nb_used);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "align scan launch");
+  if (nch > 0) {
+    align_scatter_kernel<<<nch, kChunk, sm_scatter, st>>>(ids, ids_dtype == MV_I64, P, E1, hist, start, sorted);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "align scatter launch");
+  }
+  return MV_OK;
 }
 
 }  // namespace prefill
@@ -468,12 +515,18 @@ extern "C" int mv_moe_align(const void* ids, int ids_dtype, int P, int E1, int B
     return fail(MV_ERR_INVALID, "mv_moe_align: bad P=%d / E1=%d (<= %d) / BM=%d", P, E1, kAlignMaxE1, BM);
   if ((P > 0 && ids == nullptr) || sorted_out == nullptr || bexp_out == nullptr || nb_used_out == nullptr)
     return fail(MV_ERR_INVALID, "mv_moe_align: null pointer");
-  if (workspace == nullptr || workspace_bytes < kWsHeaderBytes)
-    return fail(MV_ERR_WORKSPACE, "mv_moe_align: workspace of %zu bytes needed", kWsHeaderBytes);
+  const size_t need = mv_moe_align_workspace_bytes(P, E1);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return fail(MV_ERR_WORKSPACE, "mv_moe_align: workspace of %zu bytes needed", need);
   const long long nb_max = (static_cast<long long>(P) + static_cast<long long>(E1) * (BM - 1) + BM - 1) / BM;
   if (nb_max * BM > 0x7fffffffLL) return fail(MV_ERR_INVALID, "mv_moe_align: too many pairs");
   return launch_align(ids, ids_dtype, P, E1, BM, static_cast<int>(nb_max), sorted_out, bexp_out, nb_used_out,
+                      reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes),
                       static_cast<WsHeader*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t mv_moe_align_workspace_bytes(int P, int E1) {
+  return kWsHeaderBytes + align_scratch_bytes(P > 0 ? P : 0, E1 > 0 ? E1 : 1);
 }
 
 extern "C" size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1) {
@@ -542,7 +595,9 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
     if ((rc = make_tmap(&tm_wd, w->w_d, 3, d, s, b, "w_d")) != MV_OK) return rc;
   }
 
-  if ((rc = launch_align(ids, ids_dtype, L.P, E1, kBM, L.nb_max, sorted, bexp, nb_used, hdr, st)) != MV_OK) return rc;
+  if ((rc = launch_align(ids, ids_dtype, L.P, E1, kBM, L.nb_max, sorted, bexp, nb_used,
+                        reinterpret_cast<int*>(ws + L.off_align), hdr, st)) != MV_OK)
+    return rc;
   const int G = num_sms();
   gather_kernel<<<G * 4, 256, 0, st>>>(static_cast<const uint16_t*>(x), x_stride, sorted, nb_used, NK, L.P, H, xs,
                                        static_cast<const uint16_t*>(residual), residual_stride, y32, N);

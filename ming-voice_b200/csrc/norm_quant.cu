@@ -75,6 +75,50 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void* __restrict__ x
   }
 }
 
+// bf16 in / bf16 weight / bf16 out, n a multiple of 256 and <= 4096: one warp per row, the row held in
+// registers (16-byte loads and stores). Same arithmetic as rmsnorm_kernel: the squares of bf16 values are
+// exact in fp32 and their sum is taken in fp64, so the result does not depend on the summation order.
+template <int NV>  // 16-byte vectors per lane: n = NV * 256
+__global__ void __launch_bounds__(256) rmsnorm_bf16_warp_kernel(const uint16_t* __restrict__ x, long long x_stride,
+                                                                const uint16_t* __restrict__ w,
+                                                                uint16_t* __restrict__ y, int rows, int n, float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * x_stride);
+  uint4 v[NV];
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = xr[lane + 32 * i];
+    const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16lo(u[j]), b = bf16hi(u[j]);
+      ss += static_cast<double>(a * a) + static_cast<double>(b * b);
+    }
+  }
+  ss = warp_sum_d(ss);
+  const float var = static_cast<float>(ss / static_cast<double>(n));
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + row * n);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const uint4 wv = wr[lane + 32 * i];
+    const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = __fmul_rn(bf16lo(wu[j]), round_bf16(__fmul_rn(bf16lo(u[j]), r)));
+      const float hi = __fmul_rn(bf16hi(wu[j]), round_bf16(__fmul_rn(bf16hi(u[j]), r)));
+      o[j] = static_cast<uint32_t>(f2bf(lo)) | (static_cast<uint32_t>(f2bf(hi)) << 16);
+    }
+    yr[lane + 32 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // One warp per row: amax, scale = max(amax, 1e-8) / 127 (f32 or rounded to bf16), q = rint(w / scale).
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const void* __restrict__ w, int w_dtype,
                                                             long long w_stride, long long rows, int K,
@@ -125,8 +169,26 @@ extern "C" int mv_rmsnorm(const void* x, int x_dtype, long long x_stride, const 
     return fail(MV_ERR_UNSUPPORTED, "mv_rmsnorm: dtypes must be bf16/f16/f32");
   if (rows < 0 || n <= 0 || x_stride < n) return fail(MV_ERR_INVALID, "mv_rmsnorm: bad shape rows=%d n=%d", rows, n);
   if (rows == 0) return MV_OK;
-  rmsnorm_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, x_dtype, x_stride, w, w_dtype, y, y_dtype,
-                                                                        n, eps);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (x_dtype == MV_BF16 && w_dtype == MV_BF16 && y_dtype == MV_BF16 && n % 256 == 0 && n <= 4096 && aligned16(x) &&
+      aligned16(w) && aligned16(y) && (x_stride * 2) % 16 == 0) {
+    const unsigned int blocks = static_cast<unsigned int>((rows + 7) / 8);
+    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    const uint16_t* wb = static_cast<const uint16_t*>(w);
+    uint16_t* yb = static_cast<uint16_t*>(y);
+    switch (n / 256) {
+#define MV_RMS_CASE(NV) \
+  case NV:              \
+    rmsnorm_bf16_warp_kernel<NV><<<blocks, 256, 0, st>>>(xb, x_stride, wb, yb, rows, n, eps); \
+    break;
+      MV_RMS_CASE(1) MV_RMS_CASE(2) MV_RMS_CASE(3) MV_RMS_CASE(4) MV_RMS_CASE(5) MV_RMS_CASE(6) MV_RMS_CASE(7)
+      MV_RMS_CASE(8) MV_RMS_CASE(9) MV_RMS_CASE(10) MV_RMS_CASE(11) MV_RMS_CASE(12) MV_RMS_CASE(13)
+      MV_RMS_CASE(14) MV_RMS_CASE(15) MV_RMS_CASE(16)
+#undef MV_RMS_CASE
+    }
+    return cuda_status(cudaGetLastError(), "mv_rmsnorm launch");
+  }
+  rmsnorm_kernel<<<rows, 256, 0, st>>>(x, x_dtype, x_stride, w, w_dtype, y, y_dtype, n, eps);
   return cuda_status(cudaGetLastError(), "mv_rmsnorm launch");
 }
 

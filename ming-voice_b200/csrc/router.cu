@@ -193,6 +193,132 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const Params p) {
   }
 }
 
+// Large n, tensor-core form: fp64 MMA (m16n8k4, exact products, fp64 accumulation) over a tile of 16 tokens
+// x 64 experts per pass. The 4 warps split K into quarters; inside a warp, lane t of each quad walks its own
+// contiguous run of S = H/16 k-indices (the dot product is a sum over K, so any fixed assignment of k to the
+// MMA's k-slots gives the same terms), which lets every lane load 8 (bf16/int8) or 4 (f32) consecutive
+// values per row with one vector load. The quarters are added in warp order (deterministic).
+constexpr int kDM = 16, kDWarps = 4, kDE = 64;
+
+template <int WDT>  // MV_F32, MV_BF16 or MV_I8
+struct RowChunk {
+  static constexpr int KG = WDT == MV_F32 ? 4 : 8;  // k-values per vector load
+  uint32_t raw[WDT == MV_F32 ? 4 : (WDT == MV_BF16 ? 4 : 2)];
+  __device__ __forceinline__ void load(const void* w, long long e, int H, int k) {
+    if constexpr (WDT == MV_F32) {
+      const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const float*>(w) + e * H + k);
+      raw[0] = v.x; raw[1] = v.y; raw[2] = v.z; raw[3] = v.w;
+    } else if constexpr (WDT == MV_BF16) {
+      const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(w) + e * H + k);
+      raw[0] = v.x; raw[1] = v.y; raw[2] = v.z; raw[3] = v.w;
+    } else {
+      const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const int8_t*>(w) + e * H + k);
+      raw[0] = v.x; raw[1] = v.y;
+    }
+  }
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < static_cast<int>(sizeof(raw) / 4); ++i) raw[i] = 0u;
+  }
+  // value i of the chunk as the fp32 the oracle uses (int8: dequantised with one rounded multiply)
+  __device__ __forceinline__ float get(int i, float sc) const {
+    if (WDT == MV_F32) return __uint_as_float(raw[i]);
+    if (WDT == MV_BF16) return (i & 1) ? bf16hi(raw[i >> 1]) : bf16lo(raw[i >> 1]);
+    const int q = static_cast<int>(static_cast<int8_t>((raw[i >> 2] >> (8 * (i & 3))) & 0xffu));
+    return dequant(static_cast<float>(q), sc);
+  }
+};
+
+__device__ __forceinline__ void dmma_16x8x4(double (&c)[4], double a0, double a1, double b0) {
+  asm volatile("mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+               : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
+               : "d"(a0), "d"(a1), "d"(b0));
+}
+
+template <int WDT>
+__global__ void __launch_bounds__(128) route_logits_dmma_kernel(const Params p) {
+  constexpr int KG = RowChunk<WDT>::KG;
+  __shared__ double part[kDWarps][kDM][kDE + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int m0 = blockIdx.x * kDM;
+  const int S = p.H / 16;                          // k-values per lane
+  const int kbase = warp * (p.H / 4) + t * S;      // this lane's run
+  const int ma = m0 + g, mb = m0 + g + 8;
+  const uint16_t* xa = p.x + static_cast<long long>(ma < p.n ? ma : 0) * p.x_stride;
+  const uint16_t* xb = p.x + static_cast<long long>(mb < p.n ? mb : 0) * p.x_stride;
+  for (int e0 = 0; e0 < p.E; e0 += kDE) {
+    double acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0;
+    float sc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = e0 + 8 * j + g;
+      sc[j] = 1.0f;
+      if (WDT == MV_I8 && e < p.E)
+        sc[j] = p.scale_bf16 ? __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(p.w_scale)[e]) << 16)
+                             : static_cast<const float*>(p.w_scale)[e];
+    }
+    for (int s = 0; s < S; s += KG) {
+      const int k = kbase + s;
+      double xav[KG], xbv[KG];
+      {
+        uint32_t ra[KG / 2], rb[KG / 2];
+        if constexpr (KG == 8) {
+          const uint4 va = ma < p.n ? *reinterpret_cast<const uint4*>(xa + k) : make_uint4(0, 0, 0, 0);
+          const uint4 vb = mb < p.n ? *reinterpret_cast<const uint4*>(xb + k) : make_uint4(0, 0, 0, 0);
+          ra[0] = va.x; ra[1] = va.y; ra[2] = va.z; ra[3] = va.w;
+          rb[0] = vb.x; rb[1] = vb.y; rb[2] = vb.z; rb[3] = vb.w;
+        } else {
+          const uint2 va = ma < p.n ? *reinterpret_cast<const uint2*>(xa + k) : make_uint2(0, 0);
+          const uint2 vb = mb < p.n ? *reinterpret_cast<const uint2*>(xb + k) : make_uint2(0, 0);
+          ra[0] = va.x; ra[1] = va.y;
+          rb[0] = vb.x; rb[1] = vb.y;
+        }
+#pragma unroll
+        for (int i = 0; i < KG; ++i) {
+          xav[i] = static_cast<double>((i & 1) ? bf16hi(ra[i >> 1]) : bf16lo(ra[i >> 1]));
+          xbv[i] = static_cast<double>((i & 1) ? bf16hi(rb[i >> 1]) : bf16lo(rb[i >> 1]));
+        }
+      }
+      RowChunk<WDT> wr[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int e = e0 + 8 * j + g;
+        if (e < p.E)
+          wr[j].load(p.w, e, p.H, k);
+        else
+          wr[j].zero();
+      }
+#pragma unroll
+      for (int i = 0; i < KG; ++i) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dmma_16x8x4(acc[j], xav[i], xbv[i], static_cast<double>(wr[j].get(i, sc[j])));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      part[warp][g][8 * j + 2 * t] = acc[j][0];
+      part[warp][g][8 * j + 2 * t + 1] = acc[j][1];
+      part[warp][g + 8][8 * j + 2 * t] = acc[j][2];
+      part[warp][g + 8][8 * j + 2 * t + 1] = acc[j][3];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kDM * kDE; i += blockDim.x) {
+      const int r = i / kDE, c = i % kDE;
+      const int m = m0 + r, e = e0 + c;
+      if (m < p.n && e < p.E) {
+        double v = part[0][r][c];
+#pragma unroll
+        for (int w2 = 1; w2 < kDWarps; ++w2) v += part[w2][r][c];
+        p.logits[static_cast<long long>(m) * p.E + e] = static_cast<float>(v);
+      }
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(256) route_select_kernel(const Params p) {
   __shared__ float scr[8][kMaxE];
   const int warp = threadIdx.x >> 5;
@@ -216,8 +342,18 @@ int route_launch(const route::Params& p, cudaStream_t st, bool pdl_primary) {
     return cuda_status(cudaGetLastError(), "route_small launch");
   }
   if (p.norm_w != nullptr) return fail(MV_ERR_UNSUPPORTED, "route: fused RMSNorm only for n <= 16");
-  dim3 grid((p.n + kTM - 1) / kTM, (p.E + kTE - 1) / kTE);
-  route_logits_kernel<<<grid, 256, 0, st>>>(p);
+  if (p.H % 128 == 0 && aligned16(p.x) && (p.x_stride * 2) % 16 == 0) {
+    const unsigned int blocks = static_cast<unsigned int>((p.n + kDM - 1) / kDM);
+    if (p.w_dtype == MV_BF16)
+      route_logits_dmma_kernel<MV_BF16><<<blocks, 128, 0, st>>>(p);
+    else if (p.w_dtype == MV_F32)
+      route_logits_dmma_kernel<MV_F32><<<blocks, 128, 0, st>>>(p);
+    else
+      route_logits_dmma_kernel<MV_I8><<<blocks, 128, 0, st>>>(p);
+  } else {
+    dim3 grid((p.n + kTM - 1) / kTM, (p.E + kTE - 1) / kTE);
+    route_logits_kernel<<<grid, 256, 0, st>>>(p);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "route_logits launch");
   route_select_kernel<<<(p.n + 7) / 8, 256, 0, st>>>(p);

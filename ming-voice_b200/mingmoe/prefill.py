@@ -23,7 +23,7 @@ def align(ids: torch.Tensor, E1: int, BM: int):
     sorted_ids = torch.empty(nb_max * BM, dtype=torch.int32, device=ids.device)
     bexp = torch.empty(nb_max, dtype=torch.int32, device=ids.device)
     nb_used = torch.empty(1, dtype=torch.int32, device=ids.device)
-    ws = L.workspace("align", 256, ids.device)
+    ws = L.workspace("align", L.lib().mv_moe_align_workspace_bytes(P, E1), ids.device)
     L.check(L.lib().mv_moe_align(L.ptr(flat), L.dt(flat), P, E1, BM, L.ptr(sorted_ids), L.ptr(bexp), L.ptr(nb_used),
                                  L.ptr(ws), ws.numel(), L.stream_ptr(ids.device)), "mv_moe_align")
     return sorted_ids, bexp, nb_used
