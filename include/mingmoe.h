@@ -163,6 +163,11 @@ MV_API int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_st
                           void* workspace, size_t workspace_bytes, void* stream);
 MV_API size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1);
 
+/* Workspace for the fastest decode path (the tensor-core kernel, bf16 weights, H and I multiples of 128,
+ * H <= 2048): larger than mv_moe_decode_workspace_bytes, which is the minimum (with the minimum the CUDA-core
+ * kernel runs). Sized for M tokens with NK experts each from E1 stacked slots. */
+MV_API size_t mv_moe_decode_workspace_bytes_tc(int M, int NK, int H, int I, int E1);
+
 /* One MoE block: RMSNorm -> router -> routed + shared experts -> residual. */
 typedef struct mv_block {
   mv_moe_weights experts;   /* stacked routed experts and the shared-expert slot(s) */
@@ -193,6 +198,8 @@ typedef struct mv_block {
 MV_API int mv_block_decode(const mv_block* b, const void* x, int M, void* out, float* logits_out, void* ids_out,
                            int ids_dtype, float* wts_out, void* workspace, size_t workspace_bytes, void* stream);
 MV_API size_t mv_block_decode_workspace_bytes(int M, int n_experts_per_token, int I, int E);
+/* Workspace for the fastest mv_block_decode path for up to M tokens (see mv_moe_decode_workspace_bytes_tc). */
+MV_API size_t mv_block_decode_workspace_bytes_tc(const mv_block* b, int M);
 
 /* mv_block_decode without a caller workspace: no counterpart in the reference (its Triton launches take
  * torch-allocated buffers). For callers that cannot allocate device memory or keep a workspace -- a C/FFI

@@ -76,6 +76,17 @@ __device__ __forceinline__ double warp_sum_d(double v) {
   return v;
 }
 
+// Named barrier over `nthreads` threads that also returns the AND of `pred` over them (one decision for all).
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\tselp.s32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<int>(pred)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // Named barrier over `nthreads` threads (a multiple of 32), id 1..15 (0 is __syncthreads).
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

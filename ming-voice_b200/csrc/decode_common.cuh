@@ -1,0 +1,276 @@
+// Shared pieces of the decode kernels: the launch parameters, the expert table builders and small helpers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "route_select.cuh"
+
+namespace mv {
+namespace decode {
+
+constexpr int kStageBytes = 32768;
+constexpr int kMaxM = 16;
+constexpr int kMaxNK = 32;
+constexpr int kMaxE1 = 4096;
+constexpr int kGuSegMax = 256;  // gate/up rows per segment (int8 scale staging)
+constexpr int kNhMax = 64;      // output rows per CTA
+
+struct Params {
+  const uint8_t* w_gu;
+  const uint8_t* w_d;
+  const void* s_gu;
+  const void* s_d;
+  long long gu_se, gu_sr, d_se, d_sr, sgu_se, sd_se;  // element strides
+  int E1, H, I;
+  int s_bf16;
+  const uint16_t* x;
+  long long x_stride;
+  const uint16_t* norm_w;
+  float eps;
+  int M;
+  // mode 0: pairs given
+  const void* ids;
+  int ids_i64;
+  const float* wts;
+  int NK;
+  // mode 1: fused router
+  int router;
+  int route_mode;
+  const void* rw;
+  int rw_dtype;
+  const void* rw_scale;
+  int rw_scale_bf16;
+  const float* rbias;
+  int E, top_k, n_group, topk_group;
+  double rscale;
+  int n_static, static_id;
+  float* logits_out;
+  void* ids_out;
+  int ids_out_i64;
+  float* wts_out;
+  // outputs / workspace
+  const uint16_t* residual;
+  uint16_t* out;
+  WsHeader* ws;
+  float* logits_ws;  // [M, E]
+  float* a_g;        // [pairs, I]
+  // geometry (host-computed)
+  int n_stages;
+  int RG, DR;
+  int u_max;
+  int region_bytes;  // x / a-buffer union
+  int DP;            // w_d rows per packed down stage
+  int gsc_cap;       // gate/up scales per CTA (int8)
+  int nh_cap;        // output rows per CTA
+  int a_all;         // 1: the down phase loads every (expert, token) activation row at once
+  int E_alloc;       // selection scratch per warp (router mode)
+  // tensor-core path (decode_tc_run)
+  float* tc_part_gu;   // [items][2][M][128] gate / up partial sums (split K)
+  float* tc_part_d;    // [G * kTcMaxSeg][M][128] down-projection pieces
+  uint16_t* tc_abuf;   // [u_max * 32][I] bf16: rows 0..15 = hi(a * w) per token, 16..31 = lo
+  int* tc_cnt;         // [(u_max * (I / 128) + H / 128) * 4] arrival counters per 32-row group (zero between calls)
+  int tc_kcn_s;        // K-chunks per static (shared-expert) slice
+  int tc_kmax;         // largest power of two dividing H / 128
+};
+
+constexpr int kTcMaxSeg = 4;
+
+template <bool INT8>
+struct W;
+template <>
+struct W<false> {
+  static constexpr int esz = 2, vec = 8;
+};
+template <>
+struct W<true> {
+  static constexpr int esz = 1, vec = 16;
+};
+
+// Rows [r, hi) of a gate/up row space of `ubase`-offset experts, cut into per-expert segments.
+struct GuWalk {
+  long long r, hi;
+  int I, ubase;
+  __device__ bool next(int& u, int& i0, int& ni, long long& rpos) {
+    if (r >= hi) return false;
+    rpos = r;
+    u = ubase + static_cast<int>(r / I);
+    i0 = static_cast<int>(r % I);
+    long long n = hi - r;
+    if (n > I - i0) n = I - i0;
+    if (n > kGuSegMax) n = kGuSegMax;
+    ni = static_cast<int>(n);
+    r += n;
+    return true;
+  }
+};
+
+__device__ __forceinline__ float ldscale(const void* base, long long idx, int bf16) {
+  if (bf16) return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(base)[idx]) << 16);
+  return reinterpret_cast<const float*>(base)[idx];
+}
+
+__device__ __forceinline__ float router_w(const Params& p, long long e, int h) {
+  const long long i = e * p.H + h;
+  if (p.rw_dtype == MV_F32) return static_cast<const float*>(p.rw)[i];
+  if (p.rw_dtype == MV_BF16) return __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(p.rw)[i]) << 16);
+  const float s = ldscale(p.rw_scale, e, p.rw_scale_bf16);
+  return dequant(static_cast<float>(static_cast<const int8_t*>(p.rw)[i]), s);
+}
+
+// Expert table from (expert, weight) pairs, by ONE warp, for at most 32 pairs: lane j holds pair j; first
+// occurrences, ranks and token positions come from fully unrolled shuffle loops (no serial dependence).
+template <int MT>
+__device__ void table_warp(const int* pr_e, const float* pr_w, int npairs, int kp, int E1, int n_static, int static_id,
+                           int M, int* e_id, int* e_ntok, int* e_tok, float* e_w, int* e_pbase, int* misc, WsHeader* ws) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane;
+  const int e = j < npairs ? pr_e[j] : -1;
+  const float wj = j < npairs ? pr_w[j] : 0.f;
+  const int mj = j / kp;
+  const bool valid = j < npairs && e >= 0 && e < E1;
+  bool first = valid, newtok = valid;
+  float wsum = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int ek = __shfl_sync(0xffffffffu, e, k);
+    const float wk = __shfl_sync(0xffffffffu, wj, k);
+    const bool vk = k < npairs && ek >= 0 && ek < E1;
+    const bool same = vk && ek == e && (k / kp) == mj;
+    if (vk && k < j && ek == e) first = false;
+    if (same && k < j) newtok = false;
+    if (same) wsum += wk;
+  }
+  int rank = n_static, pos = 0, ntok = 0;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int ek = __shfl_sync(0xffffffffu, e, k);
+    const bool fk = __shfl_sync(0xffffffffu, first, k);
+    const bool nk = __shfl_sync(0xffffffffu, newtok, k);
+    if (fk && valid && ek < e) ++rank;
+    if (nk && valid && ek == e) {
+      if (k < j) ++pos;
+      ++ntok;
+    }
+  }
+  const int nfirst = __popc(__ballot_sync(0xffffffffu, first));
+  for (int u = lane; u < n_static; u += 32) {
+    e_id[u] = static_id + u;
+    e_ntok[u] = M;
+    for (int t = 0; t < M; ++t) {
+      e_tok[u * MT + t] = t;
+      e_w[u * MT + t] = 1.0f;
+    }
+  }
+  if (first) {
+    e_id[rank] = e;
+    e_ntok[rank] = ntok < MT ? ntok : MT;
+  }
+  if (newtok && pos < MT) {
+    e_tok[rank * MT + pos] = mj;
+    e_w[rank * MT + pos] = wsum;
+  }
+  if (newtok && pos >= MT) raise_error(ws, kErrOverflow, static_cast<unsigned int>(j));
+  __syncwarp();
+  if (lane == 0) {
+    const int Ut = n_static + nfirst;
+    int pb = 0;
+    for (int u = 0; u < Ut; ++u) {
+      e_pbase[u] = pb;
+      pb += e_ntok[u];
+    }
+    misc[0] = Ut;
+    misc[3] = pb;
+  }
+  __syncwarp();
+}
+
+// Expert table by NT threads (any number of pairs): bitmap of the distinct experts, a warp-0 prefix over its
+// words, then one thread per expert collecting its tokens in order.
+template <int MT, typename Sync>
+__device__ void table_bitmap(const int* pr_e, const float* pr_w, int npairs, int kp, int E1, int n_static,
+                             int static_id, int M, int* e_id, int* e_ntok, int* e_tok, float* e_w, int* e_pbase,
+                             int* misc, unsigned int* bitmap, WsHeader* ws, int t, int NT, Sync sync) {
+  const int lane = t & 31;
+  const int nwords = (E1 + 31) >> 5;
+  for (int i = t; i < nwords; i += NT) bitmap[i] = 0u;
+  sync();
+  for (int j = t; j < npairs; j += NT) {
+    const int e = pr_e[j];
+    if (e >= 0 && e < E1) atomicOr(&bitmap[e >> 5], 1u << (e & 31));
+  }
+  sync();
+  if (t < 32) {
+    int base = n_static;
+    for (int w0 = 0; w0 < nwords; w0 += 32) {
+      const int wd = w0 + lane;
+      const int c = wd < nwords ? __popc(bitmap[wd]) : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (wd < nwords) {
+        unsigned int b = bitmap[wd];
+        int r = base + incl - c;
+        while (b) {
+          e_id[r++] = (wd << 5) + __ffs(b) - 1;
+          b &= b - 1;
+        }
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) misc[0] = base;
+  }
+  for (int u = t; u < n_static; u += NT) {
+    e_id[u] = static_id + u;
+    e_ntok[u] = M;
+    for (int tt = 0; tt < M; ++tt) {
+      e_tok[u * MT + tt] = tt;
+      e_w[u * MT + tt] = 1.0f;
+    }
+  }
+  sync();
+  const int Ut = misc[0];
+  for (int u = n_static + t; u < Ut; u += NT) {
+    const int e = e_id[u];
+    int n = 0;
+    for (int j = 0; j < npairs; ++j) {
+      if (pr_e[j] != e) continue;
+      const int m = j / kp;
+      if (n > 0 && e_tok[u * MT + n - 1] == m) {
+        e_w[u * MT + n - 1] += pr_w[j];
+      } else if (n < MT) {
+        e_tok[u * MT + n] = m;
+        e_w[u * MT + n] = pr_w[j];
+        ++n;
+      } else {
+        raise_error(ws, kErrOverflow, static_cast<unsigned int>(j));
+      }
+    }
+    e_ntok[u] = n;
+  }
+  sync();
+  if (t == 0) {
+    int pb = 0;
+    for (int u = 0; u < Ut; ++u) {
+      e_pbase[u] = pb;
+      pb += e_ntok[u];
+    }
+    misc[3] = pb;
+  }
+  sync();
+}
+
+}  // namespace decode
+
+// The tensor-core decode path (bf16 weights): workspace need and launch. Returns MV_OK, an error, or
+// kDecodeTcUnsuitable when the shapes / workspace do not fit it (the caller then uses the CUDA-core kernel).
+constexpr int kDecodeTcUnsuitable = -1;
+size_t decode_tc_workspace_bytes(int M, int nk, int H, int I, int E1, int E, int n_static);
+int decode_tc_run(decode::Params& p, void* workspace, size_t workspace_bytes, int nk_pairs, cudaStream_t st);
+
+}  // namespace mv

@@ -33,111 +33,10 @@
 #include <stdint.h>
 #include <stdlib.h>
 
-#include "common.cuh"
-#include "route_select.cuh"
+#include "decode_common.cuh"
 
 namespace mv {
 namespace decode {
-
-constexpr int kStageBytes = 32768;
-constexpr int kMaxM = 16;
-constexpr int kMaxNK = 32;
-constexpr int kMaxE1 = 4096;
-constexpr int kGuSegMax = 256;  // gate/up rows per segment (int8 scale staging)
-constexpr int kNhMax = 64;      // output rows per CTA
-
-struct Params {
-  const uint8_t* w_gu;
-  const uint8_t* w_d;
-  const void* s_gu;
-  const void* s_d;
-  long long gu_se, gu_sr, d_se, d_sr, sgu_se, sd_se;  // element strides
-  int E1, H, I;
-  int s_bf16;
-  const uint16_t* x;
-  long long x_stride;
-  const uint16_t* norm_w;
-  float eps;
-  int M;
-  // mode 0: pairs given
-  const void* ids;
-  int ids_i64;
-  const float* wts;
-  int NK;
-  // mode 1: fused router
-  int router;
-  int route_mode;
-  const void* rw;
-  int rw_dtype;
-  const void* rw_scale;
-  int rw_scale_bf16;
-  const float* rbias;
-  int E, top_k, n_group, topk_group;
-  double rscale;
-  int n_static, static_id;
-  float* logits_out;
-  void* ids_out;
-  int ids_out_i64;
-  float* wts_out;
-  // outputs / workspace
-  const uint16_t* residual;
-  uint16_t* out;
-  WsHeader* ws;
-  float* logits_ws;  // [M, E]
-  float* a_g;        // [pairs, I]
-  // geometry (host-computed)
-  int n_stages;
-  int RG, DR;
-  int u_max;
-  int region_bytes;  // x / a-buffer union
-  int DP;            // w_d rows per packed down stage
-  int gsc_cap;       // gate/up scales per CTA (int8)
-  int nh_cap;        // output rows per CTA
-  int a_all;         // 1: the down phase loads every (expert, token) activation row at once
-  int E_alloc;       // selection scratch per warp (router mode)
-};
-
-template <bool INT8>
-struct W;
-template <>
-struct W<false> {
-  static constexpr int esz = 2, vec = 8;
-};
-template <>
-struct W<true> {
-  static constexpr int esz = 1, vec = 16;
-};
-
-// Rows [r, hi) of a gate/up row space of `ubase`-offset experts, cut into per-expert segments.
-struct GuWalk {
-  long long r, hi;
-  int I, ubase;
-  __device__ bool next(int& u, int& i0, int& ni, long long& rpos) {
-    if (r >= hi) return false;
-    rpos = r;
-    u = ubase + static_cast<int>(r / I);
-    i0 = static_cast<int>(r % I);
-    long long n = hi - r;
-    if (n > I - i0) n = I - i0;
-    if (n > kGuSegMax) n = kGuSegMax;
-    ni = static_cast<int>(n);
-    r += n;
-    return true;
-  }
-};
-
-__device__ __forceinline__ float ldscale(const void* base, long long idx, int bf16) {
-  if (bf16) return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(base)[idx]) << 16);
-  return reinterpret_cast<const float*>(base)[idx];
-}
-
-__device__ __forceinline__ float router_w(const Params& p, long long e, int h) {
-  const long long i = e * p.H + h;
-  if (p.rw_dtype == MV_F32) return static_cast<const float*>(p.rw)[i];
-  if (p.rw_dtype == MV_BF16) return __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(p.rw)[i]) << 16);
-  const float s = ldscale(p.rw_scale, e, p.rw_scale_bf16);
-  return dequant(static_cast<float>(static_cast<const int8_t*>(p.rw)[i]), s);
-}
 
 // 16 bytes of weights -> VEC fp32 values (int8: dequantised with scale sc)
 template <bool INT8>
@@ -166,151 +65,6 @@ template <int VEC>
 __device__ __forceinline__ int split_off(int i, int n) {
   constexpr int NQ = VEC / 4;
   return ((i % VEC) / 4) * (n / NQ) + (i / VEC) * 4 + (i & 3);
-}
-
-// Expert table from (expert, weight) pairs, by ONE warp, for at most 32 pairs: lane j holds pair j; first
-// occurrences, ranks and token positions come from fully unrolled shuffle loops (no serial dependence).
-template <int MT>
-__device__ void table_warp(const int* pr_e, const float* pr_w, int npairs, int kp, int E1, int n_static, int static_id,
-                           int M, int* e_id, int* e_ntok, int* e_tok, float* e_w, int* e_pbase, int* misc, WsHeader* ws) {
-  const int lane = threadIdx.x & 31;
-  const int j = lane;
-  const int e = j < npairs ? pr_e[j] : -1;
-  const float wj = j < npairs ? pr_w[j] : 0.f;
-  const int mj = j / kp;
-  const bool valid = j < npairs && e >= 0 && e < E1;
-  bool first = valid, newtok = valid;
-  float wsum = 0.f;
-#pragma unroll
-  for (int k = 0; k < 32; ++k) {
-    const int ek = __shfl_sync(0xffffffffu, e, k);
-    const float wk = __shfl_sync(0xffffffffu, wj, k);
-    const bool vk = k < npairs && ek >= 0 && ek < E1;
-    const bool same = vk && ek == e && (k / kp) == mj;
-    if (vk && k < j && ek == e) first = false;
-    if (same && k < j) newtok = false;
-    if (same) wsum += wk;
-  }
-  int rank = n_static, pos = 0, ntok = 0;
-#pragma unroll
-  for (int k = 0; k < 32; ++k) {
-    const int ek = __shfl_sync(0xffffffffu, e, k);
-    const bool fk = __shfl_sync(0xffffffffu, first, k);
-    const bool nk = __shfl_sync(0xffffffffu, newtok, k);
-    if (fk && valid && ek < e) ++rank;
-    if (nk && valid && ek == e) {
-      if (k < j) ++pos;
-      ++ntok;
-    }
-  }
-  const int nfirst = __popc(__ballot_sync(0xffffffffu, first));
-  for (int u = lane; u < n_static; u += 32) {
-    e_id[u] = static_id + u;
-    e_ntok[u] = M;
-    for (int t = 0; t < M; ++t) {
-      e_tok[u * MT + t] = t;
-      e_w[u * MT + t] = 1.0f;
-    }
-  }
-  if (first) {
-    e_id[rank] = e;
-    e_ntok[rank] = ntok < MT ? ntok : MT;
-  }
-  if (newtok && pos < MT) {
-    e_tok[rank * MT + pos] = mj;
-    e_w[rank * MT + pos] = wsum;
-  }
-  if (newtok && pos >= MT) raise_error(ws, kErrOverflow, static_cast<unsigned int>(j));
-  __syncwarp();
-  if (lane == 0) {
-    const int Ut = n_static + nfirst;
-    int pb = 0;
-    for (int u = 0; u < Ut; ++u) {
-      e_pbase[u] = pb;
-      pb += e_ntok[u];
-    }
-    misc[0] = Ut;
-    misc[3] = pb;
-  }
-  __syncwarp();
-}
-
-// Expert table by NT threads (any number of pairs): bitmap of the distinct experts, a warp-0 prefix over its
-// words, then one thread per expert collecting its tokens in order.
-template <int MT, typename Sync>
-__device__ void table_bitmap(const int* pr_e, const float* pr_w, int npairs, int kp, int E1, int n_static,
-                             int static_id, int M, int* e_id, int* e_ntok, int* e_tok, float* e_w, int* e_pbase,
-                             int* misc, unsigned int* bitmap, WsHeader* ws, int t, int NT, Sync sync) {
-  const int lane = t & 31;
-  const int nwords = (E1 + 31) >> 5;
-  for (int i = t; i < nwords; i += NT) bitmap[i] = 0u;
-  sync();
-  for (int j = t; j < npairs; j += NT) {
-    const int e = pr_e[j];
-    if (e >= 0 && e < E1) atomicOr(&bitmap[e >> 5], 1u << (e & 31));
-  }
-  sync();
-  if (t < 32) {
-    int base = n_static;
-    for (int w0 = 0; w0 < nwords; w0 += 32) {
-      const int wd = w0 + lane;
-      const int c = wd < nwords ? __popc(bitmap[wd]) : 0;
-      int incl = c;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
-      }
-      if (wd < nwords) {
-        unsigned int b = bitmap[wd];
-        int r = base + incl - c;
-        while (b) {
-          e_id[r++] = (wd << 5) + __ffs(b) - 1;
-          b &= b - 1;
-        }
-      }
-      base += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) misc[0] = base;
-  }
-  for (int u = t; u < n_static; u += NT) {
-    e_id[u] = static_id + u;
-    e_ntok[u] = M;
-    for (int tt = 0; tt < M; ++tt) {
-      e_tok[u * MT + tt] = tt;
-      e_w[u * MT + tt] = 1.0f;
-    }
-  }
-  sync();
-  const int Ut = misc[0];
-  for (int u = n_static + t; u < Ut; u += NT) {
-    const int e = e_id[u];
-    int n = 0;
-    for (int j = 0; j < npairs; ++j) {
-      if (pr_e[j] != e) continue;
-      const int m = j / kp;
-      if (n > 0 && e_tok[u * MT + n - 1] == m) {
-        e_w[u * MT + n - 1] += pr_w[j];
-      } else if (n < MT) {
-        e_tok[u * MT + n] = m;
-        e_w[u * MT + n] = pr_w[j];
-        ++n;
-      } else {
-        raise_error(ws, kErrOverflow, static_cast<unsigned int>(j));
-      }
-    }
-    e_ntok[u] = n;
-  }
-  sync();
-  if (t == 0) {
-    int pb = 0;
-    for (int u = 0; u < Ut; ++u) {
-      e_pbase[u] = pb;
-      pb += e_ntok[u];
-    }
-    misc[3] = pb;
-  }
-  sync();
 }
 
 template <bool INT8, int MT, int CW>
@@ -1021,6 +775,13 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
   p.I = I;
   p.s_bf16 = w->s_dtype == MV_BF16;
   p.ws = static_cast<WsHeader*>(workspace);
+  if (!int8) {  // the tensor-core kernel when the shapes and the workspace suit it
+    const char* path = getenv("MINGMOE_DECODE_PATH");
+    if (path == nullptr || path[0] != 'c') {
+      const int rc = decode_tc_run(p, workspace, workspace_bytes, nk_pairs, st);
+      if (rc != kDecodeTcUnsuitable) return rc;
+    }
+  }
   const size_t lg = (static_cast<size_t>(M) * (p.router ? p.E : 0) * 4 + 255) & ~size_t(255);
   p.logits_ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes);
   p.a_g = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes + lg);
@@ -1105,6 +866,20 @@ extern "C" size_t mv_moe_decode_workspace_bytes(int M, int NK, int I, int E) {
   E = E > 0 ? E : 0;
   const size_t lg = (static_cast<size_t>(M) * E * 4 + 255) & ~size_t(255);
   return kWsHeaderBytes + lg + static_cast<size_t>(M) * NK * I * sizeof(float);
+}
+
+extern "C" size_t mv_moe_decode_workspace_bytes_tc(int M, int NK, int H, int I, int E1) {
+  const size_t classic = mv_moe_decode_workspace_bytes(M, NK, I, 0);
+  const size_t tc = decode_tc_workspace_bytes(M, NK, H, I, E1, 0, 0);
+  return tc > classic ? tc : classic;
+}
+
+extern "C" size_t mv_block_decode_workspace_bytes_tc(const mv_block* b, int M) {
+  if (b == nullptr) return 0;
+  const int nk = b->top_k + b->n_shared;
+  const size_t classic = mv_block_decode_workspace_bytes(M, nk, b->experts.I, b->E);
+  const size_t tc = decode_tc_workspace_bytes(M, nk, b->experts.H, b->experts.I, b->experts.E1, b->E, b->n_shared);
+  return tc > classic ? tc : classic;
 }
 
 extern "C" int mv_moe_decode(const mv_moe_weights* w, const void* x, long long x_stride, const void* norm_w,

@@ -1,0 +1,891 @@
+// Decode MoE block (M <= 16 tokens, bf16 weights) on the 5th-generation tensor cores: one cooperative kernel.
+//
+// Same contract as the CUDA-core decode kernel (mv_moe_decode / mv_block_decode; reference fused_moe.py:14-83,
+// engine.py:371-386); this path runs whenever the weights are bf16, H and I are multiples of 128, H <= 2048
+// and the caller's workspace holds what it needs (decode_tc_workspace_bytes), else the CUDA-core kernel runs.
+//
+// Roles inside each CTA (one CTA per SM, 192 threads):
+//   warp 0  TMA producer: streams 32 KB weight tiles (128 rows x 128 K, two 128-byte-swizzled atoms) into a
+//           4-deep ring, never waiting for anything but free ring slots (and, once, the expert table and the
+//           grid barrier before the down phase);
+//   warp 1  MMA issuer (one thread): tcgen05.mma, M = 128 weight rows, N = 16 tokens (gate/up: A = weights,
+//           B = the normalised tokens resident in shared memory) or N = 32 (down: B = hi/lo bf16 activations),
+//           fp32 accumulators in TMEM (2 x 32 columns, double-buffered);
+//   warps 2-5 epilogue: TMEM -> registers -> global partial sums; also the prologue's router and the table.
+//
+// Work split (every SM gets an equal share of the weight bytes):
+//   gate/up  item = (expert slot j, 128-row slice s of the intermediate dimension, K-chunk kc): 128 gate rows
+//            and the matching 128 up rows over H / kcn columns. kcn (split-K factor) is the smallest power of
+//            two that gives >= 4 items per SM; the shared-expert slots (no routing needed) form their own item
+//            set, streamed while the router runs. Items go round-robin over the CTAs. Each item writes its fp32
+//            gate/up partials; the last of a slice's kcn items to finish (arrival counter) adds them in kc
+//            order, applies SiLU(gate) * up * routing weight and stores the activation as two bf16 rows
+//            (hi = bf16(v), lo = bf16(v - hi)), so the down projection sees it to ~16 bits.
+//   grid barrier (all activations stored).
+//   down     the sequence of (128-row output slice hs, expert slot j, 128-K block kd) stages is cut into G
+//            equal ranges; a CTA accumulates its range slice by slice in TMEM (the expert sum happens inside
+//            the accumulator), writes one fp32 piece per slice touched, and the last piece of a slice adds the
+//            pieces in CTA order, the hi and lo columns and the residual, and stores bf16.
+// Every sum has a fixed order, so results are deterministic. Every wait is bounded (errors in the workspace).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "decode_common.cuh"
+#include "tc.cuh"
+
+namespace mv {
+namespace dtc {
+
+using decode::Params;
+using decode::kMaxE1;
+using decode::kMaxM;
+using decode::kMaxNK;
+using decode::kTcMaxSeg;
+
+constexpr int kThreads = 192;
+constexpr int kEpi = 128;          // epilogue threads (warps 2..5)
+constexpr int kStages = 4;
+constexpr int kAStage = 32768;     // 128 rows x 128 K bf16
+constexpr int kBTile = 8192;       // 32 rows x 128 K bf16 (down-phase B)
+constexpr uint32_t kTmemCols = 64;
+constexpr int kMaxH = 2048;
+
+struct SmemLayout {
+  uint32_t ring, xb, bars, tmem, misc, e_id, e_ntok, e_pbase, e_tok, e_w, wd, bitmap, pr_e, pr_w, sel_r, sel_sc,
+      sel_gs, sel_k, red, total;
+  __host__ __device__ SmemLayout(int H, int u_max, int M, int E_alloc, int top_k) {
+    uint32_t o = 0;
+    ring = o;
+    o += kStages * kAStage;
+    xb = o;
+    const uint32_t xbb = static_cast<uint32_t>(H) * 32u;  // 16 token rows x H bf16
+    o += ((xbb > static_cast<uint32_t>(kStages * kBTile) ? xbb : kStages * kBTile) + 1023u) & ~1023u;
+    bars = o;
+    o += (2 * kStages + 6) * 8;
+    tmem = o;
+    o += 16;
+    misc = o;
+    o += 16 * 4;
+    e_id = o;
+    o += u_max * 4;
+    e_ntok = o;
+    o += u_max * 4;
+    e_pbase = o;
+    o += u_max * 4;
+    e_tok = o;
+    o += u_max * kMaxM * 4;
+    e_w = o;
+    o += u_max * kMaxM * 4;
+    wd = o;
+    o += u_max * kMaxM * 4;
+    bitmap = o;
+    o += (kMaxE1 / 32) * 4;
+    pr_e = o;
+    o += kMaxM * kMaxNK * 4;
+    pr_w = o;
+    o += kMaxM * kMaxNK * 4;
+    sel_r = o;
+    o += M * E_alloc * 4;
+    sel_sc = o;
+    o += M * E_alloc * 4;
+    sel_gs = o;
+    o += M * 32 * 4;
+    o = (o + 7u) & ~7u;
+    sel_k = o;
+    o += M * (top_k > 0 ? top_k : 1) * 8;
+    red = o;
+    o += 8 * kMaxM * 8;
+    total = o;
+  }
+};
+
+__host__ __device__ inline int kcn_for(int nslices, int kmax, int G) {
+  int k = 1;
+  while (k < kmax && nslices * k < 4 * G) k <<= 1;
+  return k;
+}
+
+// the static (shared-expert) items: the largest split that keeps them within two items per CTA
+__host__ __device__ inline int kcn_static(int nslices, int kmax, int G) {
+  int k = 1;
+  while (k < kmax && nslices * k * 2 <= 2 * G) k <<= 1;
+  return k;
+}
+
+// byte offset of the 16-byte chunk c (elements 8c..8c+7) of token row t in the swizzled B layout
+__device__ __forceinline__ uint32_t xb_off(int t, int c) {
+  return static_cast<uint32_t>((c >> 3) * 2048 + t * 128 + (((c & 7) ^ (t & 7)) << 4));
+}
+
+__device__ __forceinline__ float ldcg(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// fp64 router logits of one expert row against the (swizzled) normalised tokens; one warp.
+template <int DT>
+__device__ void router_logits_sw(const void* w_row, float sc, const uint8_t* xb, int H, int M, double (&acc)[kMaxM]) {
+  const int lane = threadIdx.x & 31;
+  constexpr int per = DT == MV_F32 ? 4 : (DT == MV_BF16 ? 8 : 16);
+  const int nch = H / per;
+  for (int c = lane; c < nch; c += 32) {
+    const uint4 wv = ld_nc_v4(static_cast<const uint8_t*>(w_row) + static_cast<size_t>(c) * 16);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    float wf[per];
+    if constexpr (DT == MV_F32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) wf[q] = __uint_as_float(ww[q]);
+    } else if constexpr (DT == MV_BF16) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        wf[2 * q] = bf16lo(ww[q]);
+        wf[2 * q + 1] = bf16hi(ww[q]);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float f0, f1, f2, f3;
+        i8x4_to_f32(ww[q], f0, f1, f2, f3);
+        wf[4 * q] = dequant(f0, sc);
+        wf[4 * q + 1] = dequant(f1, sc);
+        wf[4 * q + 2] = dequant(f2, sc);
+        wf[4 * q + 3] = dequant(f3, sc);
+      }
+    }
+    const int k0 = c * per;
+#pragma unroll
+    for (int t = 0; t < kMaxM; ++t) {
+      if (t >= M) break;
+#pragma unroll
+      for (int v = 0; v < per; v += 2) {
+        const int k = k0 + v;
+        const uint32_t xx = *reinterpret_cast<const uint32_t*>(xb + xb_off(t, k >> 3) + (k & 7) * 2);
+        acc[t] += static_cast<double>(wf[v]) * static_cast<double>(bf16lo(xx));
+        acc[t] += static_cast<double>(wf[v + 1]) * static_cast<double>(bf16hi(xx));
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_decode_tc_kernel(const Params p, const __grid_constant__ CUtensorMap tm_gu,
+                         const __grid_constant__ CUtensorMap tm_d, const __grid_constant__ CUtensorMap tm_ab) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const SmemLayout Ls(p.H, p.u_max, p.M, p.E_alloc, p.top_k);
+  uint8_t* ring = sm + Ls.ring;
+  uint8_t* xb = sm + Ls.xb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Ls.bars);
+  uint64_t* empty = full + kStages;
+  uint64_t* accf = empty + kStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* tbl = acce + 2;
+  uint64_t* done = tbl + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Ls.tmem);
+  int* misc = reinterpret_cast<int*>(sm + Ls.misc);
+  int* e_id = reinterpret_cast<int*>(sm + Ls.e_id);
+  int* e_ntok = reinterpret_cast<int*>(sm + Ls.e_ntok);
+  int* e_pbase = reinterpret_cast<int*>(sm + Ls.e_pbase);
+  int* e_tok = reinterpret_cast<int*>(sm + Ls.e_tok);
+  float* e_w = reinterpret_cast<float*>(sm + Ls.e_w);
+  float* wd = reinterpret_cast<float*>(sm + Ls.wd);
+  unsigned int* bitmap = reinterpret_cast<unsigned int*>(sm + Ls.bitmap);
+  int* pr_e = reinterpret_cast<int*>(sm + Ls.pr_e);
+  float* pr_w = reinterpret_cast<float*>(sm + Ls.pr_w);
+  float* sel_r = reinterpret_cast<float*>(sm + Ls.sel_r);
+  float* sel_sc = reinterpret_cast<float*>(sm + Ls.sel_sc);
+  float* sel_gs = reinterpret_cast<float*>(sm + Ls.sel_gs);
+  double* sel_k = reinterpret_cast<double*>(sm + Ls.sel_k);
+  double* red = reinterpret_cast<double*>(sm + Ls.red);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x, H = p.H, I = p.I, M = p.M;
+  const int S = I / 128, KB = H / 128, KD = I / 128, HS = H / 128;
+  const int n_static = p.router ? p.n_static : 0;
+  const int kmax = p.tc_kmax, kcn_s = p.tc_kcn_s;
+  const int Ns = n_static * S * kcn_s;
+  int* cnt_gu = p.tc_cnt;
+  int* cnt_d = p.tc_cnt + p.u_max * S * 4;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], kEpi);
+    }
+    mbar_init(tbl, 1);
+    mbar_init(done, 1);
+    fence_mbar_init();
+    misc[1] = 0;
+    misc[2] = 0;
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tm_gu);
+    tc::prefetch_tmap(&tm_d);
+    tc::prefetch_tmap(&tm_ab);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+
+  // ---------------------------------------------------------------- prologue: tokens -> swizzled B (all threads)
+  {
+    const int nch = H / 8;
+    for (int i = tid; i < (kMaxM - M) * nch; i += kThreads) {
+      const int t = M + i / nch, c = i % nch;
+      *reinterpret_cast<uint4*>(xb + xb_off(t, c)) = make_uint4(0, 0, 0, 0);
+    }
+    for (int m = 0; m < M; ++m) {
+      const uint4* xr = reinterpret_cast<const uint4*>(p.x + m * p.x_stride);
+      double ss = 0.0;
+      for (int c = tid; c < nch; c += kThreads) {
+        const uint4 v = xr[c];
+        *reinterpret_cast<uint4*>(xb + xb_off(m, c)) = v;
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const double a = bf16lo(vv[q]), b = bf16hi(vv[q]);
+          ss += a * a + b * b;
+        }
+      }
+      if (p.norm_w != nullptr) {
+        ss = warp_sum_d(ss);
+        if (lane == 0) red[warp * kMaxM + m] = ss;
+      }
+    }
+    if (p.norm_w != nullptr) {
+      __syncthreads();
+      const uint4* gw = reinterpret_cast<const uint4*>(p.norm_w);
+      for (int m = 0; m < M; ++m) {
+        double ss = 0.0;
+        for (int w = 0; w < kThreads / 32; ++w) ss += red[w * kMaxM + m];
+        const float var = static_cast<float>(ss / static_cast<double>(H));
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+        for (int c = tid; c < nch; c += kThreads) {
+          uint4* dst = reinterpret_cast<uint4*>(xb + xb_off(m, c));
+          const uint4 v = *dst;
+          const uint4 g = gw[c];
+          const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+          const uint32_t gg[4] = {g.x, g.y, g.z, g.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float y0 = round_bf16(__fmul_rn(bf16lo(vv[q]), r));
+            const float y1 = round_bf16(__fmul_rn(bf16hi(vv[q]), r));
+            o[q] = static_cast<uint32_t>(f2bf(__fmul_rn(bf16lo(gg[q]), y0))) |
+                   (static_cast<uint32_t>(f2bf(__fmul_rn(bf16hi(gg[q]), y1))) << 16);
+          }
+          *dst = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+  }
+  fence_proxy_async_smem();  // the tensor core reads xb through the async proxy
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  // down-phase range of this CTA (needs U: computed after the table)
+  auto d_range = [&](int U, long long& L, long long& QT, long long& q_lo, long long& q_hi) {
+    L = static_cast<long long>(U) * KD;
+    QT = HS * L;
+    q_lo = QT * blockIdx.x / G;
+    q_hi = QT * (blockIdx.x + 1) / G;
+  };
+  // first item index >= lo in this CTA's sequence blockIdx.x + k * G
+  auto first_from = [&](int lo) -> int {
+    const int b = blockIdx.x;
+    return b >= lo ? b : b + (lo - b + G - 1) / G * G;
+  };
+
+  if (warp == 0) {
+    // ================================================================ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int used[kStages];       // slot issued at least once
+      uint32_t last[kStages];  // parity of its last issue
+      for (int s = 0; s < kStages; ++s) used[s] = 0;
+      auto acquire = [&]() -> int {
+        if (ok) ok = mbar_wait(&empty[stage], ph ^ 1u, p.ws, 0x600u | stage);
+        const int s = stage;
+        used[s] = 1;
+        last[s] = ph;
+        if (++stage == kStages) {
+          stage = 0;
+          ph ^= 1u;
+        }
+        return s;
+      };
+      auto gu_item = [&](int e, int sl, int kc, int kcn) {
+        const int nkb = KB / kcn;
+        for (int half = 0; half < 2 && ok; ++half) {
+          const int row = half * I + sl * 128;
+          for (int kb = kc * nkb; kb < (kc + 1) * nkb; ++kb) {
+            const int st = acquire();
+            if (!ok) return;
+            uint8_t* dst = ring + st * kAStage;
+            mbar_arrive_expect_tx(&full[st], kAStage);
+            tc::tma_load_3d(dst, &tm_gu, &full[st], kb * 128, row, e);
+            tc::tma_load_3d(dst + 16384, &tm_gu, &full[st], kb * 128 + 64, row, e);
+          }
+        }
+      };
+      for (int idx = blockIdx.x; idx < Ns && ok; idx += G)
+        gu_item(p.static_id + idx / (S * kcn_s), (idx / kcn_s) % S, idx % kcn_s, kcn_s);
+      if (ok) ok = mbar_wait(tbl, 0u, p.ws, 0x610u);
+      const int U = misc[0];
+      const int Ur = U - n_static;
+      const int kcn_r = kcn_for(Ur * S, kmax, G);
+      const int Nr = Ur * S * kcn_r;
+      for (int idx = first_from(Ns); idx < Ns + Nr && ok; idx += G) {
+        const int r = idx - Ns;
+        gu_item(e_id[n_static + r / (S * kcn_r)], (r / kcn_r) % S, r % kcn_r, kcn_r);
+      }
+      long long L, QT, q_lo, q_hi;
+      d_range(U, L, QT, q_lo, q_hi);
+      auto d_a = [&](long long q, int st) {
+        const int hs = static_cast<int>(q / L);
+        const int rem = static_cast<int>(q - static_cast<long long>(hs) * L);
+        const int j = rem / KD, kd = rem % KD;
+        uint8_t* dst = ring + st * kAStage;
+        tc::tma_load_3d(dst, &tm_d, &full[st], kd * 128, hs * 128, e_id[j]);
+        tc::tma_load_3d(dst + 16384, &tm_d, &full[st], kd * 128 + 64, hs * 128, e_id[j]);
+      };
+      auto d_b = [&](long long q, int st) {
+        const int rem = static_cast<int>(q % L);
+        const int j = rem / KD, kd = rem % KD;
+        uint8_t* dst = xb + st * kBTile;
+        tc::tma_load_2d(dst, &tm_ab, &full[st], kd * 128, j * 32);
+        tc::tma_load_2d(dst + 4096, &tm_ab, &full[st], kd * 128 + 64, j * 32);
+      };
+      // weight tiles of the first stages run ahead of the grid barrier; their activation tiles follow it
+      const long long pre_end = q_lo + kStages < q_hi ? q_lo + kStages : q_hi;
+      int pre_slot[kStages];
+      int n_pre = 0;
+      for (long long q = q_lo; q < pre_end && ok; ++q) {
+        const int st = acquire();
+        if (!ok) break;
+        pre_slot[n_pre++] = st;
+        mbar_arrive_expect_tx(&full[st], kAStage + kBTile);
+        d_a(q, st);
+      }
+      const bool bar_ok = grid_wait(&p.ws->bar2, G, p.ws, 0x620u);
+      fence_proxy_async_global();
+      // the activation tiles of the stages already started are always issued, so every started stage completes
+      for (int i = 0; i < n_pre; ++i) d_b(q_lo + i, pre_slot[i]);
+      ok = ok && bar_ok;
+      for (long long q = pre_end; q < q_hi && ok; ++q) {
+        const int st = acquire();
+        if (!ok) break;
+        mbar_arrive_expect_tx(&full[st], kAStage + kBTile);
+        d_a(q, st);
+        d_b(q, st);
+      }
+      // copies in flight land before the CTA exits (immediate when the MMA warp consumed them)
+      for (int s = 0; s < kStages; ++s)
+        if (used[s]) mbar_wait(&full[s], last[s], p.ws, 0x630u);
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_gu = tc::idesc_bf16_f32(128, 16);
+      constexpr uint32_t id_d = tc::idesc_bf16_f32(128, 32);
+      int stage = 0, acc_i = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      auto take = [&](int& buf) -> bool {
+        buf = acc_i & 1;
+        const uint32_t aph = static_cast<uint32_t>(acc_i >> 1) & 1u;
+        ++acc_i;
+        if (ok) ok = mbar_wait(&acce[buf], aph ^ 1u, p.ws, 0x640u);
+        if (ok) tc::fence_after_sync();
+        return ok;
+      };
+      auto next_full = [&]() -> int {
+        if (ok) ok = mbar_wait(&full[stage], ph, p.ws, 0x650u | stage);
+        if (ok) tc::fence_after_sync();
+        const int s = stage;
+        if (++stage == kStages) {
+          stage = 0;
+          ph ^= 1u;
+        }
+        return s;
+      };
+      const uint32_t xb_a = smem_u32(xb);
+      auto gu_item = [&](int kc, int kcn) {
+        int buf;
+        if (!take(buf)) return;
+        const int nkb = KB / kcn;
+        for (int half = 0; half < 2 && ok; ++half) {
+          const uint32_t d = tmem + static_cast<uint32_t>(buf * 32 + half * 16);
+          for (int i = 0; i < nkb && ok; ++i) {
+            const int st = next_full();
+            if (!ok) return;
+            const uint64_t ad = tc::sw128_desc(smem_u32(ring + st * kAStage));
+            const int kb = kc * nkb + i;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t a = ad + (kk >> 2) * (16384 >> 4) + (kk & 3) * 2;
+              const uint64_t b = tc::sw128_desc(xb_a + (kb * 2 + (kk >> 2)) * 2048) + (kk & 3) * 2;
+              tc::mma_bf16(d, a, b, id_gu, (i | kk) != 0 ? 1u : 0u);
+            }
+            tc::mma_commit(&empty[st]);
+          }
+        }
+        if (ok) tc::mma_commit(&accf[buf]);
+      };
+      for (int idx = blockIdx.x; idx < Ns && ok; idx += G) gu_item(idx % kcn_s, kcn_s);
+      if (ok) ok = mbar_wait(tbl, 0u, p.ws, 0x660u);
+      const int U = misc[0];
+      const int Ur = U - n_static;
+      const int kcn_r = kcn_for(Ur * S, kmax, G);
+      const int Nr = Ur * S * kcn_r;
+      for (int idx = first_from(Ns); idx < Ns + Nr && ok; idx += G) gu_item((idx - Ns) % kcn_r, kcn_r);
+      long long L, QT, q_lo, q_hi;
+      d_range(U, L, QT, q_lo, q_hi);
+      for (long long q = q_lo; q < q_hi && ok;) {
+        const long long seg_end = (q / L + 1) * L < q_hi ? (q / L + 1) * L : q_hi;
+        int buf;
+        if (!take(buf)) break;
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * 32);
+        for (long long q0 = q; q < seg_end && ok; ++q) {
+          const int st = next_full();
+          if (!ok) break;
+          const uint64_t ad = tc::sw128_desc(smem_u32(ring + st * kAStage));
+          const uint64_t bd = tc::sw128_desc(xb_a + st * kBTile);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t a = ad + (kk >> 2) * (16384 >> 4) + (kk & 3) * 2;
+            const uint64_t b = bd + (kk >> 2) * (4096 >> 4) + (kk & 3) * 2;
+            tc::mma_bf16(d, a, b, id_d, (q != q0 || kk != 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&empty[st]);
+        }
+        if (ok) tc::mma_commit(&accf[buf]);
+      }
+      // every issued MMA retires before the TMEM is released
+      tc::mma_commit(done);
+      mbar_wait(done, 0u, p.ws, 0x670u);
+    }
+  } else {
+    // ================================================================ epilogue / router / table (warps 2..5)
+    const int et = tid - 64;
+    const int g4 = warp & 3;
+    const int row = g4 * 32 + lane;
+    auto ebar = [] { named_bar(1, kEpi); };
+    bool ok = true;
+    // The arrival counters start from zero in every call: each CTA clears a share of them before the first
+    // grid barrier, and no counter is used before that barrier (the workspace may hold anything: another
+    // call's layout, or the CUDA-core kernel's data).
+    auto zero_counters = [&]() {
+      const int ncnt = (p.u_max * S + HS) * 4;
+      for (int i = blockIdx.x * kEpi + et; i < ncnt; i += G * kEpi) p.tc_cnt[i] = 0;
+      __threadfence();
+    };
+    if (p.router) {
+      zero_counters();
+      const int e = blockIdx.x * 4 + (warp - 2);
+      if (e < p.E) {
+        double acc[kMaxM];
+#pragma unroll
+        for (int m = 0; m < kMaxM; ++m) acc[m] = 0.0;
+        const int resz = p.rw_dtype == MV_F32 ? 4 : (p.rw_dtype == MV_BF16 ? 2 : 1);
+        const void* wrow = static_cast<const uint8_t*>(p.rw) + static_cast<size_t>(e) * H * resz;
+        if (p.rw_dtype == MV_F32)
+          router_logits_sw<MV_F32>(wrow, 1.0f, xb, H, M, acc);
+        else if (p.rw_dtype == MV_BF16)
+          router_logits_sw<MV_BF16>(wrow, 1.0f, xb, H, M, acc);
+        else
+          router_logits_sw<MV_I8>(wrow, decode::ldscale(p.rw_scale, e, p.rw_scale_bf16), xb, H, M, acc);
+#pragma unroll
+        for (int m = 0; m < kMaxM; ++m) {
+          if (m < M) {
+            const double v = warp_sum_d(acc[m]);
+            if (lane == 0) p.logits_ws[m * p.E + e] = static_cast<float>(v);
+          }
+        }
+      }
+      ebar();
+      if (et == 0) {
+        grid_arrive(&p.ws->bar1);
+        if (!grid_wait(&p.ws->bar1, G, p.ws, 0x680u)) misc[1] = 1;
+      }
+      ebar();
+      const route::SelectCfg cfg{p.route_mode, p.E, p.top_k, p.n_group, p.topk_group, p.rscale, p.rbias};
+      route::select_parallel(cfg, p.logits_ws, M, et, kEpi, ebar, sel_r, sel_sc, sel_k, sel_gs, pr_e, pr_w);
+      if (blockIdx.x == 0) {  // router outputs: ids / weights with the static slots appended, logits
+        const int NKT = p.top_k + n_static;
+        for (int j = et; j < M * NKT; j += kEpi) {
+          const int m = j / NKT, k = j % NKT;
+          const long long id =
+              k < p.top_k ? pr_e[m * p.top_k + k] : static_cast<long long>(p.static_id + k - p.top_k);
+          const float wv = k < p.top_k ? pr_w[m * p.top_k + k] : 1.0f;
+          if (p.ids_out) {
+            if (p.ids_out_i64)
+              static_cast<long long*>(p.ids_out)[j] = id;
+            else
+              static_cast<int*>(p.ids_out)[j] = static_cast<int>(id);
+          }
+          if (p.wts_out) p.wts_out[j] = wv;
+        }
+        if (p.logits_out)
+          for (int j = et; j < M * p.E; j += kEpi) p.logits_out[j] = ld_cg_f32(p.logits_ws + j);
+      }
+      const int npairs = M * p.top_k;
+      if (npairs <= 32) {
+        if (warp == 2)
+          decode::table_warp<kMaxM>(pr_e, pr_w, npairs, p.top_k, p.E1, n_static, p.static_id, M, e_id, e_ntok, e_tok,
+                                    e_w, e_pbase, misc, p.ws);
+      } else {
+        decode::table_bitmap<kMaxM>(pr_e, pr_w, npairs, p.top_k, p.E1, n_static, p.static_id, M, e_id, e_ntok, e_tok,
+                                    e_w, e_pbase, misc, bitmap, p.ws, et, kEpi, ebar);
+      }
+    } else {
+      const int npairs = M * p.NK;
+      for (int j = et; j < npairs; j += kEpi) {
+        const long long e = p.ids_i64 ? reinterpret_cast<const long long*>(p.ids)[j]
+                                      : static_cast<long long>(reinterpret_cast<const int*>(p.ids)[j]);
+        const bool valid = e >= 0 && e < p.E1;
+        pr_e[j] = valid ? static_cast<int>(e) : -1;
+        pr_w[j] = p.wts[j];
+        if (!valid) raise_error(p.ws, kErrBadExpert, static_cast<unsigned int>(j));
+      }
+      ebar();
+      if (npairs <= 32) {
+        if (warp == 2)
+          decode::table_warp<kMaxM>(pr_e, pr_w, npairs, p.NK, p.E1, 0, 0, M, e_id, e_ntok, e_tok, e_w, e_pbase, misc,
+                                    p.ws);
+      } else {
+        decode::table_bitmap<kMaxM>(pr_e, pr_w, npairs, p.NK, p.E1, 0, 0, M, e_id, e_ntok, e_tok, e_w, e_pbase, misc,
+                                    bitmap, p.ws, et, kEpi, ebar);
+      }
+    }
+    ebar();
+    const int U = misc[0];
+    for (int i = et; i < U * kMaxM; i += kEpi) wd[i] = 0.f;
+    ebar();
+    for (int j = et; j < U; j += kEpi)
+      for (int i = 0; i < e_ntok[j]; ++i) wd[j * kMaxM + e_tok[j * kMaxM + i]] = e_w[j * kMaxM + i];
+    ebar();
+    if (et == 0) mbar_arrive(tbl);  // producer and MMA warps may read the table now
+    if (!p.router) {  // (in router mode the logits barrier already ordered the counter clearing)
+      zero_counters();
+      ebar();
+      if (et == 0) {
+        grid_arrive(&p.ws->bar1);
+        grid_wait(&p.ws->bar1, G, p.ws, 0x6a0u);
+      }
+      ebar();
+    }
+
+    // From here on every epilogue warp works on its own 32 TMEM lanes (rows) and its own arrival counters:
+    // no CTA-wide barrier inside the loops, so the warps never wait for one another.
+    int acc_i = 0;
+    auto take = [&](int& buf) -> bool {
+      buf = acc_i & 1;
+      const uint32_t aph = static_cast<uint32_t>(acc_i >> 1) & 1u;
+      ++acc_i;
+      ok = __all_sync(0xffffffffu, ok && mbar_wait(&accf[buf], aph, p.ws, 0x690u));
+      if (ok) tc::fence_after_sync();
+      return ok;
+    };
+    const uint32_t tlane = static_cast<uint32_t>(g4 * 32) << 16;
+    // SiLU(g) * u * weight as hi / lo bf16 rows of the activation buffer
+    auto finalize = [&](int j, int sl, const float* g, const float* u) {
+      uint16_t* ab = p.tc_abuf + static_cast<long long>(j) * 32 * I + sl * 128 + row;
+      for (int t = 0; t < M; ++t) {
+        const float a = g[t] / (1.0f + __expf(-g[t])) * u[t] * wd[j * kMaxM + t];
+        const uint16_t hi = f2bf(a);
+        const uint16_t lo = f2bf(a - __uint_as_float(static_cast<uint32_t>(hi) << 16));
+        ab[static_cast<long long>(t) * I] = hi;
+        ab[static_cast<long long>(16 + t) * I] = lo;
+      }
+    };
+    auto gu_item = [&](int idx, int j, int sl, int kc, int kcn) {
+      int buf;
+      if (!take(buf)) return;
+      uint32_t gr[16], ur[16];
+      tc::tmem_ld16(tmem + tlane + static_cast<uint32_t>(buf * 32), gr);
+      tc::tmem_ld16(tmem + tlane + static_cast<uint32_t>(buf * 32 + 16), ur);
+      tc::tmem_ld_wait();
+      tc::fence_before_sync();
+      mbar_arrive(&acce[buf]);
+      float g[kMaxM], u[kMaxM];
+#pragma unroll
+      for (int t = 0; t < kMaxM; ++t) {
+        g[t] = __uint_as_float(gr[t]);
+        u[t] = __uint_as_float(ur[t]);
+      }
+      if (kcn == 1) {
+        finalize(j, sl, g, u);
+        return;
+      }
+      float* pg = p.tc_part_gu + static_cast<long long>(idx) * 2 * M * 128;
+      for (int t = 0; t < M; ++t) {
+        pg[t * 128 + row] = g[t];
+        pg[(M + t) * 128 + row] = u[t];
+      }
+      __threadfence();
+      __syncwarp();
+      int* cnt = &cnt_gu[(j * S + sl) * 4 + g4];
+      int last = 0;
+      if (lane == 0) last = atomicAdd(cnt, 1) == kcn - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {  // this warp's 32 rows of the slice: add the kcn partials in kc order
+        __threadfence();
+        const float* p0 = p.tc_part_gu + static_cast<long long>(idx - kc) * 2 * M * 128;
+        for (int t = 0; t < M; ++t) g[t] = u[t] = 0.f;
+        for (int k = 0; k < kcn; ++k) {
+          const float* pk = p0 + static_cast<long long>(k) * 2 * M * 128;
+          for (int t = 0; t < M; ++t) {
+            g[t] += ldcg(pk + t * 128 + row);
+            u[t] += ldcg(pk + (M + t) * 128 + row);
+          }
+        }
+        finalize(j, sl, g, u);
+        if (lane == 0) *cnt = 0;
+      }
+    };
+    for (int idx = blockIdx.x; idx < Ns && ok; idx += G)
+      gu_item(idx, idx / (S * kcn_s), (idx / kcn_s) % S, idx % kcn_s, kcn_s);
+    const int Ur = U - n_static;
+    const int kcn_r = kcn_for(Ur * S, kmax, G);
+    const int Nr = Ur * S * kcn_r;
+    for (int idx = first_from(Ns); idx < Ns + Nr && ok; idx += G) {
+      const int r = idx - Ns;
+      gu_item(idx, n_static + r / (S * kcn_r), (r / kcn_r) % S, r % kcn_r, kcn_r);
+    }
+    // all activations of this CTA are stored: arrive on the grid barrier of the down phase
+    fence_proxy_async_global();
+    __threadfence();
+    ebar();
+    if (et == 0) grid_arrive(&p.ws->bar2);
+
+    long long L, QT, q_lo, q_hi;
+    d_range(U, L, QT, q_lo, q_hi);
+    auto qlo_of = [&](int b) { return QT * b / G; };
+    for (long long q = q_lo; q < q_hi && ok;) {
+      const int hs = static_cast<int>(q / L);
+      const long long seg_end = (q / L + 1) * L < q_hi ? (q / L + 1) * L : q_hi;
+      q = seg_end;
+      int buf;
+      if (!take(buf)) break;
+      uint32_t v[32];
+      tc::tmem_ld32(tmem + tlane + static_cast<uint32_t>(buf * 32), v);
+      tc::tmem_ld_wait();
+      tc::fence_before_sync();
+      mbar_arrive(&acce[buf]);
+      const int slot = blockIdx.x * kTcMaxSeg + (hs - static_cast<int>(q_lo / L));
+      float* pd = p.tc_part_d + static_cast<long long>(slot) * M * 128;
+      for (int t = 0; t < M; ++t) pd[t * 128 + row] = __uint_as_float(v[t]) + __uint_as_float(v[16 + t]);
+      __threadfence();
+      __syncwarp();
+      // the CTAs whose ranges meet slice hs, in order; the last to arrive adds their pieces
+      const long long A = static_cast<long long>(hs) * L, B = A + L;
+      int b0 = static_cast<int>(A * G / QT) - 1;
+      if (b0 < 0) b0 = 0;
+      while (b0 > 0 && qlo_of(b0) > A) --b0;
+      int* cnt = &cnt_d[hs * 4 + g4];
+      int last = 0;
+      if (lane == 0) {
+        int expect = 0;
+        for (int b = b0; b < G && qlo_of(b) < B; ++b) {
+          const long long lo = qlo_of(b), hi = qlo_of(b + 1);
+          if (hi > lo && (lo > A ? lo : A) < (hi < B ? hi : B)) ++expect;
+        }
+        last = atomicAdd(cnt, 1) == expect - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        float y[kMaxM];
+        for (int t = 0; t < M; ++t) y[t] = 0.f;
+        for (int b = b0; b < G && qlo_of(b) < B; ++b) {
+          const long long lo = qlo_of(b), hi = qlo_of(b + 1);
+          if (!(hi > lo && (lo > A ? lo : A) < (hi < B ? hi : B))) continue;
+          const float* pb =
+              p.tc_part_d + (static_cast<long long>(b) * kTcMaxSeg + (hs - static_cast<int>(lo / L))) * M * 128;
+          for (int t = 0; t < M; ++t) y[t] += ldcg(pb + t * 128 + row);
+        }
+        const int col = hs * 128 + row;
+        for (int t = 0; t < M; ++t) {
+          float o = y[t];
+          if (p.residual != nullptr) o += __uint_as_float(static_cast<uint32_t>(p.residual[t * H + col]) << 16);
+          p.out[t * H + col] = f2bf(o);
+        }
+        if (lane == 0) *cnt = 0;
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+  if (tid == 0) {  // the last CTA resets the grid-barrier counters for the next call
+    __threadfence();
+    if (atomicAdd(&p.ws->counter, 1u) == static_cast<unsigned int>(G - 1)) {
+      atomicExch(&p.ws->bar1, 0u);
+      atomicExch(&p.ws->bar2, 0u);
+      atomicExch(&p.ws->counter, 0u);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ host
+
+struct WsLayout {
+  size_t logits, cnt, part_gu, part_d, abuf, total;
+};
+
+static size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
+
+static int kmax_of(int H) {
+  int kb = H / 128, k = 1;
+  while (k * 2 <= kb && kb % (k * 2) == 0) k *= 2;
+  return k;
+}
+
+static WsLayout ws_layout(int M, int u_max, int n_static, int u_r_max, int H, int I, int E, int G) {
+  WsLayout L{};
+  const int S = I / 128, HS = H / 128, kmax = kmax_of(H);
+  const int kcn_s = n_static > 0 ? kcn_static(n_static * S, kmax, G) : 1;
+  long long items = 0;
+  for (int ur = 0; ur <= u_r_max; ++ur) {
+    const long long n = static_cast<long long>(n_static) * S * kcn_s + static_cast<long long>(ur) * S * kcn_for(ur * S, kmax, G);
+    if (n > items) items = n;
+  }
+  size_t o = kWsHeaderBytes;
+  L.logits = o;
+  o = up256(o + static_cast<size_t>(M) * (E > 0 ? E : 1) * 4);
+  L.cnt = o;
+  o = up256(o + static_cast<size_t>(u_max * S + HS) * 4 * 4);
+  L.part_gu = o;
+  o = up256(o + static_cast<size_t>(items) * 2 * M * 128 * 4);
+  L.part_d = o;
+  o = up256(o + static_cast<size_t>(G) * kTcMaxSeg * M * 128 * 4);
+  L.abuf = o;
+  o = up256(o + static_cast<size_t>(u_max) * 32 * I * 2);
+  L.total = o;
+  return L;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+static bool tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                 const uint32_t* box) {
+  auto enc = encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
+             reinterpret_cast<const cuuint64_t*>(dims), reinterpret_cast<const cuuint64_t*>(strides),
+             reinterpret_cast<const cuuint32_t*>(box), estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace dtc
+
+static bool tc_shapes_ok(int H, int I) { return H % 128 == 0 && I % 128 == 0 && H <= dtc::kMaxH && H >= 128; }
+
+size_t decode_tc_workspace_bytes(int M, int nk, int H, int I, int E1, int E, int n_static) {
+  if (!tc_shapes_ok(H, I) || M < 1 || M > decode::kMaxM || nk < 1) return 0;
+  const int routed = E > 0 ? nk - n_static : nk;  // experts chosen per token by the router (or given)
+  int u_r_max = M * (routed > 0 ? routed : 1);
+  const int pool = E > 0 ? E : E1;
+  if (u_r_max > pool) u_r_max = pool;
+  const int ns = E > 0 ? n_static : 0;
+  const int u_max = ns + u_r_max;
+  return dtc::ws_layout(M, u_max, ns, u_r_max, H, I, E, num_sms()).total;
+}
+
+int decode_tc_run(decode::Params& p, void* workspace, size_t workspace_bytes, int nk_pairs, cudaStream_t st) {
+  using namespace dtc;
+  const int H = p.H, I = p.I, M = p.M, G = num_sms();
+  if (!tc_shapes_ok(H, I) || p.w_gu == nullptr) return kDecodeTcUnsuitable;
+  const int n_static = p.router ? p.n_static : 0;
+  const int routed = p.router ? p.top_k : nk_pairs;
+  int u_r_max = M * routed;
+  const int pool = p.router ? p.E : p.E1;
+  if (u_r_max > pool) u_r_max = pool;
+  const int u_max = n_static + u_r_max;
+  const WsLayout L = ws_layout(M, u_max, n_static, u_r_max, H, I, p.router ? p.E : 0, G);
+  if (workspace_bytes < L.total) return kDecodeTcUnsuitable;
+  if ((H / 128 + G - 1) / G + 1 > decode::kTcMaxSeg) return kDecodeTcUnsuitable;
+  const int E_alloc = p.router ? p.E : 0;
+  const SmemLayout Ls(H, u_max, M, E_alloc, p.router ? p.top_k : 1);
+  const size_t smem = Ls.total + 1024;
+  if (smem > 227 * 1024) return kDecodeTcUnsuitable;
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.ws = reinterpret_cast<WsHeader*>(ws);
+  p.logits_ws = reinterpret_cast<float*>(ws + L.logits);
+  p.tc_cnt = reinterpret_cast<int*>(ws + L.cnt);
+  p.tc_part_gu = reinterpret_cast<float*>(ws + L.part_gu);
+  p.tc_part_d = reinterpret_cast<float*>(ws + L.part_d);
+  p.tc_abuf = reinterpret_cast<uint16_t*>(ws + L.abuf);
+  p.u_max = u_max;
+  p.E_alloc = E_alloc;
+  p.tc_kmax = kmax_of(H);
+  p.tc_kcn_s = n_static > 0 ? kcn_static(n_static * (I / 128), p.tc_kmax, G) : 1;
+  if (!p.router) p.top_k = 1;  // selection scratch sizing only
+
+  CUtensorMap tm_gu, tm_d, tm_ab;
+  {
+    const uint64_t d[3] = {static_cast<uint64_t>(H), static_cast<uint64_t>(2 * I), static_cast<uint64_t>(p.E1)};
+    const uint64_t s[2] = {static_cast<uint64_t>(p.gu_sr) * 2, static_cast<uint64_t>(p.gu_se) * 2};
+    const uint32_t b[3] = {64, 128, 1};
+    if (!tmap(&tm_gu, p.w_gu, 3, d, s, b)) return kDecodeTcUnsuitable;
+  }
+  {
+    const uint64_t d[3] = {static_cast<uint64_t>(I), static_cast<uint64_t>(H), static_cast<uint64_t>(p.E1)};
+    const uint64_t s[2] = {static_cast<uint64_t>(p.d_sr) * 2, static_cast<uint64_t>(p.d_se) * 2};
+    const uint32_t b[3] = {64, 128, 1};
+    if (!tmap(&tm_d, p.w_d, 3, d, s, b)) return kDecodeTcUnsuitable;
+  }
+  {
+    const uint64_t d[2] = {static_cast<uint64_t>(I), static_cast<uint64_t>(u_max) * 32};
+    const uint64_t s[1] = {static_cast<uint64_t>(I) * 2};
+    const uint32_t b[2] = {64, 32};
+    if (!tmap(&tm_ab, p.tc_abuf, 2, d, s, b)) return kDecodeTcUnsuitable;
+  }
+  cudaError_t e = cudaFuncSetAttribute(moe_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(moe_decode_tc)");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, moe_decode_tc_kernel, p, tm_gu, tm_d, tm_ab);
+  return cuda_status(e, "moe_decode_tc launch");
+}
+
+}  // namespace mv

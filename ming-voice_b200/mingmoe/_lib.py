@@ -59,6 +59,8 @@ _SIGS = {
     "mv_moe_decode_workspace_bytes": (SZ, [I32, I32, I32, I32]),
     "mv_block_decode": (I32, [C.POINTER(Block), P, I32, P, P, P, I32, P, P, SZ, P]),
     "mv_block_decode_workspace_bytes": (SZ, [I32, I32, I32, I32]),
+    "mv_block_decode_workspace_bytes_tc": (SZ, [C.POINTER(Block), I32]),
+    "mv_moe_decode_workspace_bytes_tc": (SZ, [I32, I32, I32, I32, I32]),
     "mv_block_decode_noalloc": (I32, [C.POINTER(Block), P, I32, P, P, P, I32, P, P, P]),
     "mv_moe_align": (I32, [P, I32, I32, I32, I32, P, P, P, P, SZ, P]),
     "mv_moe_align_workspace_bytes": (SZ, [I32, I32]),

@@ -75,7 +75,7 @@ class MoeBlock:
 
     # ------------------------------------------------------------------------------------------ decode
     def workspace_bytes(self, M=moe.DECODE_MAX_M):
-        return L.lib().mv_block_decode_workspace_bytes(M, self.nk, self.I, self.E)
+        return L.lib().mv_block_decode_workspace_bytes_tc(C.byref(self._block), M)
 
     def decode(self, x, out=None, logits=None, ids=None, wts=None):
         """h + MoE(rms_norm(h)) for M <= 16 tokens in one kernel. x [M, H] bf16. Optional router outputs are

@@ -73,7 +73,7 @@ def decode(x, w_gu, w_d, ids, wts, out=None, s_gu=None, s_d=None, norm_w=None, e
     y = torch.empty(M, H, dtype=torch.bfloat16, device=x.device) if out is None else out
     if residual is not None:
         residual = residual.reshape(M, H).contiguous()
-    nbytes = L.lib().mv_moe_decode_workspace_bytes(DECODE_MAX_M, max(ids2.shape[1], 16), ws_w.I, 0)
+    nbytes = L.lib().mv_moe_decode_workspace_bytes_tc(DECODE_MAX_M, max(ids2.shape[1], 16), ws_w.H, ws_w.I, ws_w.E1)
     ws = L.workspace("decode", nbytes, x.device)
     L.check(L.lib().mv_moe_decode(C.byref(ws_w), L.ptr(x), x.stride(0), L.ptr(norm_w), float(eps), L.ptr(ids2),
                                   L.dt(ids2), L.ptr(w2), M, ids2.shape[1], L.ptr(residual), L.ptr(y), L.ptr(ws),

@@ -206,3 +206,27 @@ def test_block_prefill_small(cuda, base_params, N):
     y_ref, _, _, _ = O.moe_block(x, p, top_k=6)
     close(blk.prefill(x.to(cuda)), y_ref)
     no_device_errors()
+
+
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_decode_tensor_core_and_cuda_core_paths_agree(cuda, base_params, M):
+    """bf16 blocks run on the tcgen05 kernel; MINGMOE_DECODE_PATH=classic forces the CUDA-core kernel."""
+    import os
+    from mingmoe.block import MoeBlock
+    p = base_params
+    blk = MoeBlock.from_params(p)
+    x = O.make_tokens(M, seed=40 + M).to(cuda)
+    y_ref, ids_ref, _, _ = O.moe_block(x.cpu(), p, top_k=6)
+    ids_tc = torch.empty(M, 8, dtype=torch.long, device=cuda)
+    y_tc = blk.decode(x, ids=ids_tc)
+    os.environ["MINGMOE_DECODE_PATH"] = "classic"
+    try:
+        ids_cc = torch.empty(M, 8, dtype=torch.long, device=cuda)
+        y_cc = blk.decode(x, ids=ids_cc)
+    finally:
+        del os.environ["MINGMOE_DECODE_PATH"]
+    assert torch.equal(ids_tc, ids_cc) and torch.equal(ids_tc.cpu(), ids_ref)
+    close(y_tc, y_ref)
+    close(y_cc, y_ref)
+    close(y_tc, y_cc.float(), max_abs=1.6e-2)
+    no_device_errors()
