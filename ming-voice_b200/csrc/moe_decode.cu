@@ -721,6 +721,12 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
 
 using decode::Params;
 
+// Token count from which the tensor-core kernel (moe_decode_tc.cu) takes over: below it the step is pure
+// weight streaming with little arithmetic, and this CUDA-core kernel's row-granular split (no split-K
+// partial sums to combine across CTAs) measured faster; from 4 tokens on the tensor cores win (3x at 8-16).
+// MINGMOE_DECODE_PATH=classic / =tc forces either kernel.
+constexpr int kTcMinM = 4;
+
 // Geometry, validation and the cooperative launch; shared by mv_moe_decode and mv_block_decode.
 int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t workspace_bytes, int nk_pairs,
                cudaStream_t st) {
@@ -775,9 +781,10 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
   p.I = I;
   p.s_bf16 = w->s_dtype == MV_BF16;
   p.ws = static_cast<WsHeader*>(workspace);
-  if (!int8) {  // the tensor-core kernel when the shapes and the workspace suit it
+  if (!int8) {  // the tensor-core kernel when the shapes and the workspace suit it (M >= 4; see kTcMinM)
     const char* path = getenv("MINGMOE_DECODE_PATH");
-    if (path == nullptr || path[0] != 'c') {
+    const bool force_tc = path != nullptr && path[0] == 't';
+    if ((path == nullptr || path[0] != 'c') && (M >= kTcMinM || force_tc)) {
       const int rc = decode_tc_run(p, workspace, workspace_bytes, nk_pairs, st);
       if (rc != kDecodeTcUnsuitable) return rc;
     }

@@ -42,13 +42,15 @@ using decode::kMaxM;
 using decode::kMaxNK;
 using decode::kTcMaxSeg;
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 256;
 constexpr int kEpi = 128;          // epilogue threads (warps 2..5)
+constexpr int kRt = 64;            // router / table threads (warps 6..7)
 constexpr int kStages = 4;
 constexpr int kAStage = 32768;     // 128 rows x 128 K bf16
 constexpr int kBTile = 8192;       // 32 rows x 128 K bf16 (down-phase B)
 constexpr uint32_t kTmemCols = 64;
 constexpr int kMaxH = 2048;
+constexpr int kMaxPieces = 32;   // CTA ranges that can meet one 128-row output slice: <= G / (H / 128) + 2
 
 struct SmemLayout {
   uint32_t ring, xb, bars, tmem, misc, e_id, e_ntok, e_pbase, e_tok, e_w, wd, bitmap, pr_e, pr_w, sel_r, sel_sc,
@@ -125,15 +127,25 @@ __device__ __forceinline__ float ldcg(const float* p) {
 
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// fp64 router logits of one expert row against the (swizzled) normalised tokens; one warp.
+// fp64 router logits of one expert row against the (swizzled) normalised tokens; one warp. All of the lane's
+// row chunks are loaded before any is used (the row reads then cost one memory latency, not H / 256).
 template <int DT>
 __device__ void router_logits_sw(const void* w_row, float sc, const uint8_t* xb, int H, int M, double (&acc)[kMaxM]) {
   const int lane = threadIdx.x & 31;
   constexpr int per = DT == MV_F32 ? 4 : (DT == MV_BF16 ? 8 : 16);
+  constexpr int kMaxCh = kMaxH / per / 32;  // chunks per lane at H = kMaxH
   const int nch = H / per;
-  for (int c = lane; c < nch; c += 32) {
-    const uint4 wv = ld_nc_v4(static_cast<const uint8_t*>(w_row) + static_cast<size_t>(c) * 16);
-    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint4 buf[kMaxCh];
+#pragma unroll
+  for (int i = 0; i < kMaxCh; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nch) buf[i] = ld_nc_v4(static_cast<const uint8_t*>(w_row) + static_cast<size_t>(c) * 16);
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxCh; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= nch) break;
+    const uint32_t ww[4] = {buf[i].x, buf[i].y, buf[i].z, buf[i].w};
     float wf[per];
     if constexpr (DT == MV_F32) {
 #pragma unroll
@@ -312,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t ph = 0;
       bool ok = true;
+      const uint64_t pol = policy_evict_first();  // weights are read once per call: keep L2 for the rest
       int used[kStages];       // slot issued at least once
       uint32_t last[kStages];  // parity of its last issue
       for (int s = 0; s < kStages; ++s) used[s] = 0;
@@ -335,8 +348,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) return;
             uint8_t* dst = ring + st * kAStage;
             mbar_arrive_expect_tx(&full[st], kAStage);
-            tc::tma_load_3d(dst, &tm_gu, &full[st], kb * 128, row, e);
-            tc::tma_load_3d(dst + 16384, &tm_gu, &full[st], kb * 128 + 64, row, e);
+            tc::tma_load_3d_hint(dst, &tm_gu, &full[st], kb * 128, row, e, pol);
+            tc::tma_load_3d_hint(dst + 16384, &tm_gu, &full[st], kb * 128 + 64, row, e, pol);
           }
         }
       };
@@ -358,8 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rem = static_cast<int>(q - static_cast<long long>(hs) * L);
         const int j = rem / KD, kd = rem % KD;
         uint8_t* dst = ring + st * kAStage;
-        tc::tma_load_3d(dst, &tm_d, &full[st], kd * 128, hs * 128, e_id[j]);
-        tc::tma_load_3d(dst + 16384, &tm_d, &full[st], kd * 128 + 64, hs * 128, e_id[j]);
+        tc::tma_load_3d_hint(dst, &tm_d, &full[st], kd * 128, hs * 128, e_id[j], pol);
+        tc::tma_load_3d_hint(dst + 16384, &tm_d, &full[st], kd * 128 + 64, hs * 128, e_id[j], pol);
       };
       auto d_b = [&](long long q, int st) {
         const int rem = static_cast<int>(q % L);
@@ -477,24 +490,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mma_commit(done);
       mbar_wait(done, 0u, p.ws, 0x670u);
     }
-  } else {
-    // ================================================================ epilogue / router / table (warps 2..5)
-    const int et = tid - 64;
-    const int g4 = warp & 3;
-    const int row = g4 * 32 + lane;
-    auto ebar = [] { named_bar(1, kEpi); };
-    bool ok = true;
-    // The arrival counters start from zero in every call: each CTA clears a share of them before the first
-    // grid barrier, and no counter is used before that barrier (the workspace may hold anything: another
-    // call's layout, or the CUDA-core kernel's data).
-    auto zero_counters = [&]() {
+  } else if (warp >= 6) {
+    // ================================================================ router / table (warps 6..7)
+    const int rt = tid - 192;
+    auto rbar = [] { named_bar(2, kRt); };
+    // the arrival counters start from zero in every call (the workspace may hold anything: another call's
+    // layout, or the CUDA-core kernel's data): each CTA clears a share, then a grid barrier publishes it
+    {
       const int ncnt = (p.u_max * S + HS) * 4;
-      for (int i = blockIdx.x * kEpi + et; i < ncnt; i += G * kEpi) p.tc_cnt[i] = 0;
+      for (int i = blockIdx.x * kRt + rt; i < ncnt; i += G * kRt) p.tc_cnt[i] = 0;
       __threadfence();
-    };
+      rbar();
+      if (rt == 0) grid_arrive(&p.ws->pad[0]);
+    }
     if (p.router) {
-      zero_counters();
-      const int e = blockIdx.x * 4 + (warp - 2);
+      const int e = blockIdx.x * 2 + (warp - 6);
       if (e < p.E) {
         double acc[kMaxM];
 #pragma unroll
@@ -515,17 +525,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      ebar();
-      if (et == 0) {
+      rbar();
+      if (rt == 0) {
         grid_arrive(&p.ws->bar1);
-        if (!grid_wait(&p.ws->bar1, G, p.ws, 0x680u)) misc[1] = 1;
+        grid_wait(&p.ws->bar1, G, p.ws, 0x680u);
       }
-      ebar();
+      rbar();
       const route::SelectCfg cfg{p.route_mode, p.E, p.top_k, p.n_group, p.topk_group, p.rscale, p.rbias};
-      route::select_parallel(cfg, p.logits_ws, M, et, kEpi, ebar, sel_r, sel_sc, sel_k, sel_gs, pr_e, pr_w);
+      route::select_parallel(cfg, p.logits_ws, M, rt, kRt, rbar, sel_r, sel_sc, sel_k, sel_gs, pr_e, pr_w);
       if (blockIdx.x == 0) {  // router outputs: ids / weights with the static slots appended, logits
         const int NKT = p.top_k + n_static;
-        for (int j = et; j < M * NKT; j += kEpi) {
+        for (int j = rt; j < M * NKT; j += kRt) {
           const int m = j / NKT, k = j % NKT;
           const long long id =
               k < p.top_k ? pr_e[m * p.top_k + k] : static_cast<long long>(p.static_id + k - p.top_k);
@@ -539,20 +549,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.wts_out) p.wts_out[j] = wv;
         }
         if (p.logits_out)
-          for (int j = et; j < M * p.E; j += kEpi) p.logits_out[j] = ld_cg_f32(p.logits_ws + j);
+          for (int j = rt; j < M * p.E; j += kRt) p.logits_out[j] = ld_cg_f32(p.logits_ws + j);
       }
       const int npairs = M * p.top_k;
       if (npairs <= 32) {
-        if (warp == 2)
+        if (warp == 6)
           decode::table_warp<kMaxM>(pr_e, pr_w, npairs, p.top_k, p.E1, n_static, p.static_id, M, e_id, e_ntok, e_tok,
                                     e_w, e_pbase, misc, p.ws);
       } else {
         decode::table_bitmap<kMaxM>(pr_e, pr_w, npairs, p.top_k, p.E1, n_static, p.static_id, M, e_id, e_ntok, e_tok,
-                                    e_w, e_pbase, misc, bitmap, p.ws, et, kEpi, ebar);
+                                    e_w, e_pbase, misc, bitmap, p.ws, rt, kRt, rbar);
       }
     } else {
       const int npairs = M * p.NK;
-      for (int j = et; j < npairs; j += kEpi) {
+      for (int j = rt; j < npairs; j += kRt) {
         const long long e = p.ids_i64 ? reinterpret_cast<const long long*>(p.ids)[j]
                                       : static_cast<long long>(reinterpret_cast<const int*>(p.ids)[j]);
         const bool valid = e >= 0 && e < p.E1;
@@ -560,36 +570,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         pr_w[j] = p.wts[j];
         if (!valid) raise_error(p.ws, kErrBadExpert, static_cast<unsigned int>(j));
       }
-      ebar();
+      rbar();
       if (npairs <= 32) {
-        if (warp == 2)
+        if (warp == 6)
           decode::table_warp<kMaxM>(pr_e, pr_w, npairs, p.NK, p.E1, 0, 0, M, e_id, e_ntok, e_tok, e_w, e_pbase, misc,
                                     p.ws);
       } else {
         decode::table_bitmap<kMaxM>(pr_e, pr_w, npairs, p.NK, p.E1, 0, 0, M, e_id, e_ntok, e_tok, e_w, e_pbase, misc,
-                                    bitmap, p.ws, et, kEpi, ebar);
+                                    bitmap, p.ws, rt, kRt, rbar);
       }
     }
-    ebar();
+    rbar();
     const int U = misc[0];
-    for (int i = et; i < U * kMaxM; i += kEpi) wd[i] = 0.f;
-    ebar();
-    for (int j = et; j < U; j += kEpi)
+    for (int i = rt; i < U * kMaxM; i += kRt) wd[i] = 0.f;
+    rbar();
+    for (int j = rt; j < U; j += kRt)
       for (int i = 0; i < e_ntok[j]; ++i) wd[j * kMaxM + e_tok[j * kMaxM + i]] = e_w[j * kMaxM + i];
-    ebar();
-    if (et == 0) mbar_arrive(tbl);  // producer and MMA warps may read the table now
-    if (!p.router) {  // (in router mode the logits barrier already ordered the counter clearing)
-      zero_counters();
-      ebar();
-      if (et == 0) {
-        grid_arrive(&p.ws->bar1);
-        grid_wait(&p.ws->bar1, G, p.ws, 0x6a0u);
+    rbar();
+    if (rt == 0) mbar_arrive(tbl);  // producer, MMA and epilogue warps may read the table now
+  } else {
+    // ================================================================ epilogue (warps 2..5)
+    // Every epilogue warp works on its own 32 TMEM lanes (rows) and its own arrival counters: no CTA-wide
+    // barrier inside the loops, so the warps never wait for one another.
+    const int et = tid - 64;
+    const int g4 = warp & 3;
+    const int row = g4 * 32 + lane;
+    bool ok = true;
+    bool cnt_ready = false;  // the counter-clearing grid barrier has been seen by this warp
+    auto counters_ready = [&]() {
+      if (!cnt_ready) {
+        bool good = true;
+        if (lane == 0) good = grid_wait(&p.ws->pad[0], G, p.ws, 0x6a0u);
+        ok = ok && __shfl_sync(0xffffffffu, good, 0) != 0;
+        cnt_ready = true;
       }
-      ebar();
-    }
-
-    // From here on every epilogue warp works on its own 32 TMEM lanes (rows) and its own arrival counters:
-    // no CTA-wide barrier inside the loops, so the warps never wait for one another.
+    };
     int acc_i = 0;
     auto take = [&](int& buf) -> bool {
       buf = acc_i & 1;
@@ -600,11 +615,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       return ok;
     };
     const uint32_t tlane = static_cast<uint32_t>(g4 * 32) << 16;
-    // SiLU(g) * u * weight as hi / lo bf16 rows of the activation buffer
+    // SiLU(g) * u * weight as hi / lo bf16 rows of the activation buffer (static slots carry weight 1)
     auto finalize = [&](int j, int sl, const float* g, const float* u) {
       uint16_t* ab = p.tc_abuf + static_cast<long long>(j) * 32 * I + sl * 128 + row;
       for (int t = 0; t < M; ++t) {
-        const float a = g[t] / (1.0f + __expf(-g[t])) * u[t] * wd[j * kMaxM + t];
+        const float w = j < n_static ? 1.0f : wd[j * kMaxM + t];
+        const float a = g[t] / (1.0f + __expf(-g[t])) * u[t] * w;
         const uint16_t hi = f2bf(a);
         const uint16_t lo = f2bf(a - __uint_as_float(static_cast<uint32_t>(hi) << 16));
         ab[static_cast<long long>(t) * I] = hi;
@@ -637,27 +653,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __threadfence();
       __syncwarp();
+      counters_ready();
+      if (!ok) return;
       int* cnt = &cnt_gu[(j * S + sl) * 4 + g4];
       int last = 0;
       if (lane == 0) last = atomicAdd(cnt, 1) == kcn - 1;
       last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {  // this warp's 32 rows of the slice: add the kcn partials in kc order
+      if (last) {  // this warp's 32 rows of the slice: add the kcn partials in kc order, 16 loads in flight
         __threadfence();
         const float* p0 = p.tc_part_gu + static_cast<long long>(idx - kc) * 2 * M * 128;
         for (int t = 0; t < M; ++t) g[t] = u[t] = 0.f;
-        for (int k = 0; k < kcn; ++k) {
-          const float* pk = p0 + static_cast<long long>(k) * 2 * M * 128;
-          for (int t = 0; t < M; ++t) {
-            g[t] += ldcg(pk + t * 128 + row);
-            u[t] += ldcg(pk + (M + t) * 128 + row);
+        const int tot = kcn * M;
+        for (int b0 = 0; b0 < tot; b0 += 16) {
+          float lg[16], lu[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int id = b0 + i;
+            if (id < tot) {
+              const int k = id / M, t = id - k * M;
+              const float* pk = p0 + static_cast<long long>(k) * 2 * M * 128;
+              lg[i] = ldcg(pk + t * 128 + row);
+              lu[i] = ldcg(pk + (M + t) * 128 + row);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int id = b0 + i;
+            if (id < tot) {
+              const int t = id % M;
+              g[t] += lg[i];
+              u[t] += lu[i];
+            }
           }
         }
         finalize(j, sl, g, u);
-        if (lane == 0) *cnt = 0;
       }
     };
     for (int idx = blockIdx.x; idx < Ns && ok; idx += G)
       gu_item(idx, idx / (S * kcn_s), (idx / kcn_s) % S, idx % kcn_s, kcn_s);
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(tbl, 0u, p.ws, 0x6b0u));
+    const int U = misc[0];
     const int Ur = U - n_static;
     const int kcn_r = kcn_for(Ur * S, kmax, G);
     const int Nr = Ur * S * kcn_r;
@@ -665,10 +700,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r = idx - Ns;
       gu_item(idx, n_static + r / (S * kcn_r), (r / kcn_r) % S, r % kcn_r, kcn_r);
     }
+    counters_ready();  // (the down phase uses counters too)
     // all activations of this CTA are stored: arrive on the grid barrier of the down phase
     fence_proxy_async_global();
     __threadfence();
-    ebar();
+    named_bar(1, kEpi);
     if (et == 0) grid_arrive(&p.ws->bar2);
 
     long long L, QT, q_lo, q_hi;
@@ -695,27 +731,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       int b0 = static_cast<int>(A * G / QT) - 1;
       if (b0 < 0) b0 = 0;
       while (b0 > 0 && qlo_of(b0) > A) --b0;
+      int pieces[kMaxPieces];  // slot of each contributing piece, in CTA order (host-checked bound)
+      int np = 0;
+      for (int b = b0; b < G && qlo_of(b) < B && np < kMaxPieces; ++b) {
+        const long long lo = qlo_of(b), hi = qlo_of(b + 1);
+        if (hi > lo && (lo > A ? lo : A) < (hi < B ? hi : B)) pieces[np++] = b * kTcMaxSeg + (hs - static_cast<int>(lo / L));
+      }
       int* cnt = &cnt_d[hs * 4 + g4];
       int last = 0;
-      if (lane == 0) {
-        int expect = 0;
-        for (int b = b0; b < G && qlo_of(b) < B; ++b) {
-          const long long lo = qlo_of(b), hi = qlo_of(b + 1);
-          if (hi > lo && (lo > A ? lo : A) < (hi < B ? hi : B)) ++expect;
-        }
-        last = atomicAdd(cnt, 1) == expect - 1;
-      }
+      if (lane == 0) last = atomicAdd(cnt, 1) == np - 1;
       last = __shfl_sync(0xffffffffu, last, 0);
       if (last) {
         __threadfence();
         float y[kMaxM];
         for (int t = 0; t < M; ++t) y[t] = 0.f;
-        for (int b = b0; b < G && qlo_of(b) < B; ++b) {
-          const long long lo = qlo_of(b), hi = qlo_of(b + 1);
-          if (!(hi > lo && (lo > A ? lo : A) < (hi < B ? hi : B))) continue;
-          const float* pb =
-              p.tc_part_d + (static_cast<long long>(b) * kTcMaxSeg + (hs - static_cast<int>(lo / L))) * M * 128;
-          for (int t = 0; t < M; ++t) y[t] += ldcg(pb + t * 128 + row);
+        const int tot = np * M;
+        for (int c0 = 0; c0 < tot; c0 += 16) {
+          float lv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int id = c0 + i;
+            if (id < tot) {
+              const int k = id / M, t = id - k * M;
+              lv[i] = ldcg(p.tc_part_d + static_cast<long long>(pieces[k]) * M * 128 + t * 128 + row);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int id = c0 + i;
+            if (id < tot) y[id % M] += lv[i];
+          }
         }
         const int col = hs * 128 + row;
         for (int t = 0; t < M; ++t) {
@@ -723,7 +768,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.residual != nullptr) o += __uint_as_float(static_cast<uint32_t>(p.residual[t * H + col]) << 16);
           p.out[t * H + col] = f2bf(o);
         }
-        if (lane == 0) *cnt = 0;
       }
     }
   }
@@ -740,6 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (atomicAdd(&p.ws->counter, 1u) == static_cast<unsigned int>(G - 1)) {
       atomicExch(&p.ws->bar1, 0u);
       atomicExch(&p.ws->bar2, 0u);
+      atomicExch(&p.ws->pad[0], 0u);
       atomicExch(&p.ws->counter, 0u);
     }
   }
@@ -834,6 +879,7 @@ int decode_tc_run(decode::Params& p, void* workspace, size_t workspace_bytes, in
   const WsLayout L = ws_layout(M, u_max, n_static, u_r_max, H, I, p.router ? p.E : 0, G);
   if (workspace_bytes < L.total) return kDecodeTcUnsuitable;
   if ((H / 128 + G - 1) / G + 1 > decode::kTcMaxSeg) return kDecodeTcUnsuitable;
+  if ((G + H / 128 - 1) / (H / 128) + 2 > kMaxPieces) return kDecodeTcUnsuitable;
   const int E_alloc = p.router ? p.E : 0;
   const SmemLayout Ls(H, u_max, M, E_alloc, p.router ? p.top_k : 1);
   const size_t smem = Ls.total + 1024;

@@ -210,15 +210,19 @@ def test_block_prefill_small(cuda, base_params, N):
 
 @pytest.mark.parametrize("M", [1, 5, 16])
 def test_decode_tensor_core_and_cuda_core_paths_agree(cuda, base_params, M):
-    """bf16 blocks run on the tcgen05 kernel; MINGMOE_DECODE_PATH=classic forces the CUDA-core kernel."""
+    """MINGMOE_DECODE_PATH=tc / =classic force the tcgen05 or the CUDA-core kernel: both match the oracle."""
     import os
     from mingmoe.block import MoeBlock
     p = base_params
     blk = MoeBlock.from_params(p)
     x = O.make_tokens(M, seed=40 + M).to(cuda)
     y_ref, ids_ref, _, _ = O.moe_block(x.cpu(), p, top_k=6)
-    ids_tc = torch.empty(M, 8, dtype=torch.long, device=cuda)
-    y_tc = blk.decode(x, ids=ids_tc)
+    os.environ["MINGMOE_DECODE_PATH"] = "tc"
+    try:
+        ids_tc = torch.empty(M, 8, dtype=torch.long, device=cuda)
+        y_tc = blk.decode(x, ids=ids_tc)
+    finally:
+        del os.environ["MINGMOE_DECODE_PATH"]
     os.environ["MINGMOE_DECODE_PATH"] = "classic"
     try:
         ids_cc = torch.empty(M, 8, dtype=torch.long, device=cuda)
