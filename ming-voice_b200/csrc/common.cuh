@@ -182,6 +182,25 @@ static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Ws
   }
 }
 
+// The same for waits that are expected to be long (a phase of another warp's work, not a ring slot): the
+// spinning thread backs off with __nanosleep (64 ns doubling up to max_sleep_ns) so that it leaves the
+// SM's issue slots to the warps doing the work.
+static __device__ __noinline__ bool mbar_wait_lazy(uint64_t* bar, uint32_t parity, WsHeader* h, unsigned int info,
+                                                   unsigned int max_sleep_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  unsigned int ns = 64;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(ns);
+    if (ns < max_sleep_ns) ns *= 2;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_error(h, kErrTimeout, info);
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------ bulk copies
 
 // 1-D bulk copy global -> shared (TMA engine), completion counted on `bar` in bytes. `src`, `dst` 16-byte
@@ -234,8 +253,10 @@ __device__ __forceinline__ void grid_arrive(unsigned int* ctr) {
 static __device__ __noinline__ bool grid_wait(unsigned int* ctr, unsigned int target, WsHeader* h, unsigned int info) {
   if (ld_acquire_u32(ctr) >= target) return true;
   const uint64_t t0 = globaltimer_ns();
+  unsigned int ns = 32;
   while (ld_acquire_u32(ctr) < target) {
-    __nanosleep(32);
+    __nanosleep(ns);
+    if (ns < 256) ns *= 2;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       raise_error(h, kErrTimeout, info);
       return false;

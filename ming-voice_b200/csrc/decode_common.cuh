@@ -68,12 +68,10 @@ struct Params {
   int a_all;         // 1: the down phase loads every (expert, token) activation row at once
   int E_alloc;       // selection scratch per warp (router mode)
   // tensor-core path (decode_tc_run)
-  float* tc_part_gu;   // [items][2][M][128] gate / up partial sums (split K)
+  float* tc_part_gu;   // [G][2 sequences][8 segments][2][M][128] gate / up pieces of slices cut by range ends
   float* tc_part_d;    // [G * kTcMaxSeg][M][128] down-projection pieces
   uint16_t* tc_abuf;   // [u_max * 32][I] bf16: rows 0..15 = hi(a * w) per token, 16..31 = lo
   int* tc_cnt;         // [(u_max * (I / 128) + H / 128) * 4] arrival counters per 32-row group (zero between calls)
-  int tc_kcn_s;        // K-chunks per static (shared-expert) slice
-  int tc_kmax;         // largest power of two dividing H / 128
 };
 
 constexpr int kTcMaxSeg = 4;

@@ -13,19 +13,18 @@
 //           fp32 accumulators in TMEM (2 x 32 columns, double-buffered);
 //   warps 2-5 epilogue: TMEM -> registers -> global partial sums; also the prologue's router and the table.
 //
-// Work split (every SM gets an equal share of the weight bytes):
-//   gate/up  item = (expert slot j, 128-row slice s of the intermediate dimension, K-chunk kc): 128 gate rows
-//            and the matching 128 up rows over H / kcn columns. kcn (split-K factor) is the smallest power of
-//            two that gives >= 4 items per SM; the shared-expert slots (no routing needed) form their own item
-//            set, streamed while the router runs. Items go round-robin over the CTAs. Each item writes its fp32
-//            gate/up partials; the last of a slice's kcn items to finish (arrival counter) adds them in kc
-//            order, applies SiLU(gate) * up * routing weight and stores the activation as two bf16 rows
-//            (hi = bf16(v), lo = bf16(v - hi)), so the down projection sees it to ~16 bits.
+// Work split (every SM gets an equal share of the weight bytes; two sync-light sequences per phase):
+//   gate/up  elements (slice z = (expert slot j, 128 rows of the intermediate dimension), 128-K block kb): the
+//            gate tile and the up tile of slice z at kb. The shared-expert slots (no routing needed) form one
+//            sequence, streamed while the router runs; the routed slots another. Each sequence is cut into G
+//            equal contiguous ranges; a CTA accumulates its range slice by slice in TMEM. A slice inside one
+//            range is finished at once; a slice cut by a range boundary leaves fp32 pieces, and the last piece
+//            to arrive (per-slice arrival counter) adds them in CTA order. Then SiLU(gate) * up * routing weight
+//            is stored as two bf16 rows (hi = bf16(v), lo = bf16(v - hi)), so the down projection sees ~16 bits.
 //   grid barrier (all activations stored).
-//   down     the sequence of (128-row output slice hs, expert slot j, 128-K block kd) stages is cut into G
-//            equal ranges; a CTA accumulates its range slice by slice in TMEM (the expert sum happens inside
-//            the accumulator), writes one fp32 piece per slice touched, and the last piece of a slice adds the
-//            pieces in CTA order, the hi and lo columns and the residual, and stores bf16.
+//   down     the same scheme over (128-row output slice hs, expert slot j, 128-K block kd) stages: a CTA's range
+//            accumulates in TMEM (the expert sum happens inside the accumulator), and the last piece of a slice
+//            adds the pieces in CTA order, the hi and lo columns and the residual, and stores bf16.
 // Every sum has a fixed order, so results are deterministic. Every wait is bounded (errors in the workspace).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -50,11 +49,12 @@ constexpr int kAStage = 32768;     // 128 rows x 128 K bf16
 constexpr int kBTile = 8192;       // 32 rows x 128 K bf16 (down-phase B)
 constexpr uint32_t kTmemCols = 64;
 constexpr int kMaxH = 2048;
-constexpr int kMaxPieces = 32;   // CTA ranges that can meet one 128-row output slice: <= G / (H / 128) + 2
+constexpr int kMaxPieces = 32;   // CTA ranges that can meet one slice (host-checked)
+constexpr int kGuMaxSeg = 8;     // gate/up segments of one CTA in one sequence (host-checked)
 
 struct SmemLayout {
   uint32_t ring, xb, bars, tmem, misc, e_id, e_ntok, e_pbase, e_tok, e_w, wd, bitmap, pr_e, pr_w, sel_r, sel_sc,
-      sel_gs, sel_k, red, total;
+      total;
   __host__ __device__ SmemLayout(int H, int u_max, int M, int E_alloc, int top_k) {
     uint32_t o = 0;
     ring = o;
@@ -90,28 +90,38 @@ struct SmemLayout {
     o += M * E_alloc * 4;
     sel_sc = o;
     o += M * E_alloc * 4;
-    sel_gs = o;
-    o += M * 32 * 4;
-    o = (o + 7u) & ~7u;
-    sel_k = o;
-    o += M * (top_k > 0 ? top_k : 1) * 8;
-    red = o;
-    o += 8 * kMaxM * 8;
     total = o;
+    (void)top_k;
   }
 };
 
-__host__ __device__ inline int kcn_for(int nslices, int kmax, int G) {
-  int k = 1;
-  while (k < kmax && nslices * k < 4 * G) k <<= 1;
-  return k;
+// Pieces of one slice: the CTAs b (in order) whose contiguous range [T*b/G, T*(b+1)/G) of a sequence of T
+// elements meets [A, A + Lseg); b wrote its piece to slot (b * nseq + seq) * maxseg + (index of the slice
+// among the slices that b's range touches).
+__device__ __forceinline__ int first_piece_cta(long long T, long long A, int G) {
+  int b0 = static_cast<int>(A * G / T) - 1;
+  if (b0 < 0) b0 = 0;
+  while (b0 > 0 && T * b0 / G > A) --b0;
+  return b0;
 }
 
-// the static (shared-expert) items: the largest split that keeps them within two items per CTA
-__host__ __device__ inline int kcn_static(int nslices, int kmax, int G) {
-  int k = 1;
-  while (k < kmax && nslices * k * 2 <= 2 * G) k <<= 1;
-  return k;
+__device__ __forceinline__ bool meets(long long T, int b, int G, long long A, long long B) {
+  const long long lo = T * b / G, hi = T * (b + 1) / G;
+  return hi > lo && (lo > A ? lo : A) < (hi < B ? hi : B);
+}
+
+__device__ __forceinline__ int count_pieces(long long T, long long A, long long Lseg, int G) {
+  int np = 0;
+  for (int b = first_piece_cta(T, A, G); b < G && T * b / G < A + Lseg; ++b) np += meets(T, b, G, A, A + Lseg);
+  return np;
+}
+
+template <typename F>
+__device__ __forceinline__ void for_each_piece(long long T, long long A, long long Lseg, int G, int nseq, int seq,
+                                               int maxseg, F f) {
+  for (int b = first_piece_cta(T, A, G); b < G && T * b / G < A + Lseg; ++b)
+    if (meets(T, b, G, A, A + Lseg))
+      f((b * nseq + seq) * maxseg + static_cast<int>(A / Lseg - (T * b / G) / Lseg));
 }
 
 // byte offset of the 16-byte chunk c (elements 8c..8c+7) of token row t in the swizzled B layout
@@ -209,16 +219,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* pr_w = reinterpret_cast<float*>(sm + Ls.pr_w);
   float* sel_r = reinterpret_cast<float*>(sm + Ls.sel_r);
   float* sel_sc = reinterpret_cast<float*>(sm + Ls.sel_sc);
-  float* sel_gs = reinterpret_cast<float*>(sm + Ls.sel_gs);
-  double* sel_k = reinterpret_cast<double*>(sm + Ls.sel_k);
-  double* red = reinterpret_cast<double*>(sm + Ls.red);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, H = p.H, I = p.I, M = p.M;
   const int S = I / 128, KB = H / 128, KD = I / 128, HS = H / 128;
   const int n_static = p.router ? p.n_static : 0;
-  const int kmax = p.tc_kmax, kcn_s = p.tc_kcn_s;
-  const int Ns = n_static * S * kcn_s;
+  const long long T_s = static_cast<long long>(n_static) * S * KB;  // static gate/up elements
   int* cnt_gu = p.tc_cnt;
   int* cnt_d = p.tc_cnt + p.u_max * S * 4;
 
@@ -249,38 +255,44 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---------------------------------------------------------------- prologue: tokens -> swizzled B (all threads)
   {
-    const int nch = H / 8;
+    const int nch = H / 8;  // 16-byte chunks per token row
     for (int i = tid; i < (kMaxM - M) * nch; i += kThreads) {
       const int t = M + i / nch, c = i % nch;
       *reinterpret_cast<uint4*>(xb + xb_off(t, c)) = make_uint4(0, 0, 0, 0);
     }
-    for (int m = 0; m < M; ++m) {
-      const uint4* xr = reinterpret_cast<const uint4*>(p.x + m * p.x_stride);
-      double ss = 0.0;
-      for (int c = tid; c < nch; c += kThreads) {
-        const uint4 v = xr[c];
-        *reinterpret_cast<uint4*>(xb + xb_off(m, c)) = v;
-        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+    // every token's chunks in flight together (8 loads per thread before any store)
+    const int tot = M * nch;
+    for (int i0 = tid; i0 < tot; i0 += 8 * kThreads) {
+      uint4 v[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const double a = bf16lo(vv[q]), b = bf16hi(vv[q]);
-          ss += a * a + b * b;
-        }
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kThreads;
+        if (i < tot) v[u] = reinterpret_cast<const uint4*>(p.x + (i / nch) * p.x_stride)[i % nch];
       }
-      if (p.norm_w != nullptr) {
-        ss = warp_sum_d(ss);
-        if (lane == 0) red[warp * kMaxM + m] = ss;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kThreads;
+        if (i < tot) *reinterpret_cast<uint4*>(xb + xb_off(i / nch, i % nch)) = v[u];
       }
     }
-    if (p.norm_w != nullptr) {
+    if (p.norm_w != nullptr) {  // one warp per token: fp64 sum of squares (exact), then the normalisation
       __syncthreads();
       const uint4* gw = reinterpret_cast<const uint4*>(p.norm_w);
-      for (int m = 0; m < M; ++m) {
+      for (int m = warp; m < M; m += kThreads / 32) {
         double ss = 0.0;
-        for (int w = 0; w < kThreads / 32; ++w) ss += red[w * kMaxM + m];
+        for (int c = lane; c < nch; c += 32) {
+          const uint4 v = *reinterpret_cast<const uint4*>(xb + xb_off(m, c));
+          const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const double a = bf16lo(vv[q]), b = bf16hi(vv[q]);
+            ss += a * a + b * b;
+          }
+        }
+        ss = warp_sum_d(ss);
         const float var = static_cast<float>(ss / static_cast<double>(H));
         const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
-        for (int c = tid; c < nch; c += kThreads) {
+        for (int c = lane; c < nch; c += 32) {
           uint4* dst = reinterpret_cast<uint4*>(xb + xb_off(m, c));
           const uint4 v = *dst;
           const uint4 g = gw[c];
@@ -312,12 +324,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     q_lo = QT * blockIdx.x / G;
     q_hi = QT * (blockIdx.x + 1) / G;
   };
-  // first item index >= lo in this CTA's sequence blockIdx.x + k * G
-  auto first_from = [&](int lo) -> int {
-    const int b = blockIdx.x;
-    return b >= lo ? b : b + (lo - b + G - 1) / G * G;
-  };
-
   if (warp == 0) {
     // ================================================================ TMA producer
     if (lane == 0) {
@@ -339,31 +345,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return s;
       };
-      auto gu_item = [&](int e, int sl, int kc, int kcn) {
-        const int nkb = KB / kcn;
-        for (int half = 0; half < 2 && ok; ++half) {
-          const int row = half * I + sl * 128;
-          for (int kb = kc * nkb; kb < (kc + 1) * nkb; ++kb) {
+      // gate/up: this CTA's contiguous range of the (slice z, k-block) sequence; one element = the gate tile
+      // and the up tile of slice z at k-block kb
+      auto gu_range = [&](long long T, int zbase, bool is_static) {
+        const long long lo = T * blockIdx.x / G, hi = T * (blockIdx.x + 1) / G;
+        for (long long q = lo; q < hi && ok; ++q) {
+          const int z = zbase + static_cast<int>(q / KB), kb = static_cast<int>(q % KB);
+          const int j = z / S, sl = z % S;
+          const int e = is_static ? p.static_id + j : e_id[j];
+          for (int half = 0; half < 2 && ok; ++half) {
             const int st = acquire();
             if (!ok) return;
             uint8_t* dst = ring + st * kAStage;
+            const int row = half * I + sl * 128;
             mbar_arrive_expect_tx(&full[st], kAStage);
             tc::tma_load_3d_hint(dst, &tm_gu, &full[st], kb * 128, row, e, pol);
             tc::tma_load_3d_hint(dst + 16384, &tm_gu, &full[st], kb * 128 + 64, row, e, pol);
           }
         }
       };
-      for (int idx = blockIdx.x; idx < Ns && ok; idx += G)
-        gu_item(p.static_id + idx / (S * kcn_s), (idx / kcn_s) % S, idx % kcn_s, kcn_s);
-      if (ok) ok = mbar_wait(tbl, 0u, p.ws, 0x610u);
+      gu_range(T_s, 0, true);
+      if (ok) ok = mbar_wait_lazy(tbl, 0u, p.ws, 0x610u, 1024);
       const int U = misc[0];
-      const int Ur = U - n_static;
-      const int kcn_r = kcn_for(Ur * S, kmax, G);
-      const int Nr = Ur * S * kcn_r;
-      for (int idx = first_from(Ns); idx < Ns + Nr && ok; idx += G) {
-        const int r = idx - Ns;
-        gu_item(e_id[n_static + r / (S * kcn_r)], (r / kcn_r) % S, r % kcn_r, kcn_r);
-      }
+      gu_range(static_cast<long long>(U - n_static) * S * KB, n_static * S, false);
       long long L, QT, q_lo, q_hi;
       d_range(U, L, QT, q_lo, q_hi);
       auto d_a = [&](long long q, int st) {
@@ -435,35 +439,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         return s;
       };
       const uint32_t xb_a = smem_u32(xb);
-      auto gu_item = [&](int kc, int kcn) {
-        int buf;
-        if (!take(buf)) return;
-        const int nkb = KB / kcn;
-        for (int half = 0; half < 2 && ok; ++half) {
-          const uint32_t d = tmem + static_cast<uint32_t>(buf * 32 + half * 16);
-          for (int i = 0; i < nkb && ok; ++i) {
-            const int st = next_full();
-            if (!ok) return;
-            const uint64_t ad = tc::sw128_desc(smem_u32(ring + st * kAStage));
-            const int kb = kc * nkb + i;
+      auto gu_range = [&](long long T) {
+        const long long lo = T * blockIdx.x / G, hi = T * (blockIdx.x + 1) / G;
+        for (long long q = lo; q < hi && ok;) {
+          const long long seg_end = (q / KB + 1) * KB < hi ? (q / KB + 1) * KB : hi;
+          int buf;
+          if (!take(buf)) break;
+          for (long long q0 = q; q < seg_end && ok; ++q) {
+            const int kb = static_cast<int>(q % KB);
+            for (int half = 0; half < 2 && ok; ++half) {
+              const uint32_t d = tmem + static_cast<uint32_t>(buf * 32 + half * 16);
+              const int st = next_full();
+              if (!ok) break;
+              const uint64_t ad = tc::sw128_desc(smem_u32(ring + st * kAStage));
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t a = ad + (kk >> 2) * (16384 >> 4) + (kk & 3) * 2;
-              const uint64_t b = tc::sw128_desc(xb_a + (kb * 2 + (kk >> 2)) * 2048) + (kk & 3) * 2;
-              tc::mma_bf16(d, a, b, id_gu, (i | kk) != 0 ? 1u : 0u);
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint64_t a = ad + (kk >> 2) * (16384 >> 4) + (kk & 3) * 2;
+                const uint64_t b = tc::sw128_desc(xb_a + (kb * 2 + (kk >> 2)) * 2048) + (kk & 3) * 2;
+                tc::mma_bf16(d, a, b, id_gu, (q != q0 || kk != 0) ? 1u : 0u);
+              }
+              tc::mma_commit(&empty[st]);
             }
-            tc::mma_commit(&empty[st]);
           }
+          if (ok) tc::mma_commit(&accf[buf]);
         }
-        if (ok) tc::mma_commit(&accf[buf]);
       };
-      for (int idx = blockIdx.x; idx < Ns && ok; idx += G) gu_item(idx % kcn_s, kcn_s);
-      if (ok) ok = mbar_wait(tbl, 0u, p.ws, 0x660u);
+      gu_range(T_s);
+      if (ok) ok = mbar_wait_lazy(tbl, 0u, p.ws, 0x660u, 1024);
       const int U = misc[0];
-      const int Ur = U - n_static;
-      const int kcn_r = kcn_for(Ur * S, kmax, G);
-      const int Nr = Ur * S * kcn_r;
-      for (int idx = first_from(Ns); idx < Ns + Nr && ok; idx += G) gu_item((idx - Ns) % kcn_r, kcn_r);
+      gu_range(static_cast<long long>(U - n_static) * S * KB);
       long long L, QT, q_lo, q_hi;
       d_range(U, L, QT, q_lo, q_hi);
       for (long long q = q_lo; q < q_hi && ok;) {
@@ -488,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every issued MMA retires before the TMEM is released
       tc::mma_commit(done);
-      mbar_wait(done, 0u, p.ws, 0x670u);
+      mbar_wait_lazy(done, 0u, p.ws, 0x670u, 256);
     }
   } else if (warp >= 6) {
     // ================================================================ router / table (warps 6..7)
@@ -526,13 +530,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       rbar();
-      if (rt == 0) {
-        grid_arrive(&p.ws->bar1);
-        grid_wait(&p.ws->bar1, G, p.ws, 0x680u);
-      }
+      if (rt == 0) grid_arrive(&p.ws->bar1);
+      if (rt == 0) grid_wait(&p.ws->bar1, G, p.ws, 0x680u);
+      rbar();
+      // one warp per token: the logits (published by other CTAs: read through L2) into shared memory, then
+      // the selection (largest first, ties to the lower id) and the weights
+      for (int i = rt; i < M * p.E; i += kRt) sel_r[i] = ld_cg_f32(p.logits_ws + i);
       rbar();
       const route::SelectCfg cfg{p.route_mode, p.E, p.top_k, p.n_group, p.topk_group, p.rscale, p.rbias};
-      route::select_parallel(cfg, p.logits_ws, M, rt, kRt, rbar, sel_r, sel_sc, sel_k, sel_gs, pr_e, pr_w);
+      for (int t = warp - 6; t < M; t += kRt / 32)
+        route::select_core(cfg, sel_r + t * p.E, sel_sc + t * p.E, pr_e + t * p.top_k, pr_w + t * p.top_k);
+      rbar();
       if (blockIdx.x == 0) {  // router outputs: ids / weights with the static slots appended, logits
         const int NKT = p.top_k + n_static;
         for (int j = rt; j < M * NKT; j += kRt) {
@@ -610,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       buf = acc_i & 1;
       const uint32_t aph = static_cast<uint32_t>(acc_i >> 1) & 1u;
       ++acc_i;
-      ok = __all_sync(0xffffffffu, ok && mbar_wait(&accf[buf], aph, p.ws, 0x690u));
+      ok = __all_sync(0xffffffffu, ok && mbar_wait_lazy(&accf[buf], aph, p.ws, 0x690u, 256));
       if (ok) tc::fence_after_sync();
       return ok;
     };
@@ -618,7 +626,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // SiLU(g) * u * weight as hi / lo bf16 rows of the activation buffer (static slots carry weight 1)
     auto finalize = [&](int j, int sl, const float* g, const float* u) {
       uint16_t* ab = p.tc_abuf + static_cast<long long>(j) * 32 * I + sl * 128 + row;
-      for (int t = 0; t < M; ++t) {
+#pragma unroll
+      for (int t = 0; t < kMaxM; ++t) {
+        if (t >= M) break;
         const float w = j < n_static ? 1.0f : wd[j * kMaxM + t];
         const float a = g[t] / (1.0f + __expf(-g[t])) * u[t] * w;
         const uint16_t hi = f2bf(a);
@@ -627,79 +637,79 @@ __global__ void __launch_bounds__(kThreads, 1)
         ab[static_cast<long long>(16 + t) * I] = lo;
       }
     };
-    auto gu_item = [&](int idx, int j, int sl, int kc, int kcn) {
-      int buf;
-      if (!take(buf)) return;
-      uint32_t gr[16], ur[16];
-      tc::tmem_ld16(tmem + tlane + static_cast<uint32_t>(buf * 32), gr);
-      tc::tmem_ld16(tmem + tlane + static_cast<uint32_t>(buf * 32 + 16), ur);
-      tc::tmem_ld_wait();
-      tc::fence_before_sync();
-      mbar_arrive(&acce[buf]);
-      float g[kMaxM], u[kMaxM];
+    // one gate/up segment of this CTA's range: a whole slice finalizes at once; a part of a slice writes its
+    // partial sums, and the last of the slice's pieces to arrive adds them in CTA order and finalizes
+    auto gu_range = [&](long long T, int zbase, int seq) {
+      const long long lo = T * blockIdx.x / G, hi = T * (blockIdx.x + 1) / G;
+      int seg = 0;
+      for (long long q = lo; q < hi && ok; ++seg) {
+        const int zl = static_cast<int>(q / KB);
+        const long long zs = static_cast<long long>(zl) * KB;
+        const long long seg_end = zs + KB < hi ? zs + KB : hi;
+        const bool whole = q == zs && seg_end == zs + KB;
+        q = seg_end;
+        int buf;
+        if (!take(buf)) break;
+        uint32_t gr[16], ur[16];
+        tc::tmem_ld16(tmem + tlane + static_cast<uint32_t>(buf * 32), gr);
+        tc::tmem_ld16(tmem + tlane + static_cast<uint32_t>(buf * 32 + 16), ur);
+        tc::tmem_ld_wait();
+        tc::fence_before_sync();
+        mbar_arrive(&acce[buf]);
+        float g[kMaxM], u[kMaxM];
 #pragma unroll
-      for (int t = 0; t < kMaxM; ++t) {
-        g[t] = __uint_as_float(gr[t]);
-        u[t] = __uint_as_float(ur[t]);
-      }
-      if (kcn == 1) {
-        finalize(j, sl, g, u);
-        return;
-      }
-      float* pg = p.tc_part_gu + static_cast<long long>(idx) * 2 * M * 128;
-      for (int t = 0; t < M; ++t) {
-        pg[t * 128 + row] = g[t];
-        pg[(M + t) * 128 + row] = u[t];
-      }
-      __threadfence();
-      __syncwarp();
-      counters_ready();
-      if (!ok) return;
-      int* cnt = &cnt_gu[(j * S + sl) * 4 + g4];
-      int last = 0;
-      if (lane == 0) last = atomicAdd(cnt, 1) == kcn - 1;
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {  // this warp's 32 rows of the slice: add the kcn partials in kc order, 16 loads in flight
-        __threadfence();
-        const float* p0 = p.tc_part_gu + static_cast<long long>(idx - kc) * 2 * M * 128;
-        for (int t = 0; t < M; ++t) g[t] = u[t] = 0.f;
-        const int tot = kcn * M;
-        for (int b0 = 0; b0 < tot; b0 += 16) {
-          float lg[16], lu[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int id = b0 + i;
-            if (id < tot) {
-              const int k = id / M, t = id - k * M;
-              const float* pk = p0 + static_cast<long long>(k) * 2 * M * 128;
-              lg[i] = ldcg(pk + t * 128 + row);
-              lu[i] = ldcg(pk + (M + t) * 128 + row);
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int id = b0 + i;
-            if (id < tot) {
-              const int t = id % M;
-              g[t] += lg[i];
-              u[t] += lu[i];
-            }
-          }
+        for (int t = 0; t < kMaxM; ++t) {
+          g[t] = __uint_as_float(gr[t]);
+          u[t] = __uint_as_float(ur[t]);
         }
-        finalize(j, sl, g, u);
+        const int z = zbase + zl, j = z / S, sl = z % S;
+        if (whole) {
+          finalize(j, sl, g, u);
+          continue;
+        }
+        float* pg = p.tc_part_gu + (static_cast<long long>(blockIdx.x * 2 + seq) * kGuMaxSeg + seg) * 2 * M * 128;
+#pragma unroll
+        for (int t = 0; t < kMaxM; ++t) {
+          if (t >= M) break;
+          pg[t * 128 + row] = g[t];
+          pg[(M + t) * 128 + row] = u[t];
+        }
+        __threadfence();
+        __syncwarp();
+        counters_ready();
+        if (!ok) break;
+        const int np = count_pieces(T, zs, KB, G);
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&cnt_gu[z * 4 + g4], 1) == np - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {  // this warp's 32 rows of the slice: add the pieces in CTA order (a piece's loads in flight together)
+          __threadfence();
+#pragma unroll
+          for (int t = 0; t < kMaxM; ++t) g[t] = u[t] = 0.f;
+          for_each_piece(T, zs, KB, G, 2, seq, kGuMaxSeg, [&](int slot) {
+            const float* pk = p.tc_part_gu + static_cast<long long>(slot) * 2 * M * 128;
+            float lg[kMaxM], lu[kMaxM];
+#pragma unroll
+            for (int t = 0; t < kMaxM; ++t)
+              if (t < M) {
+                lg[t] = ldcg(pk + t * 128 + row);
+                lu[t] = ldcg(pk + (M + t) * 128 + row);
+              }
+#pragma unroll
+            for (int t = 0; t < kMaxM; ++t)
+              if (t < M) {
+                g[t] += lg[t];
+                u[t] += lu[t];
+              }
+          });
+          finalize(j, sl, g, u);
+        }
       }
     };
-    for (int idx = blockIdx.x; idx < Ns && ok; idx += G)
-      gu_item(idx, idx / (S * kcn_s), (idx / kcn_s) % S, idx % kcn_s, kcn_s);
-    ok = __all_sync(0xffffffffu, ok && mbar_wait(tbl, 0u, p.ws, 0x6b0u));
+    gu_range(T_s, 0, 0);
+    ok = __all_sync(0xffffffffu, ok && mbar_wait_lazy(tbl, 0u, p.ws, 0x6b0u, 1024));
     const int U = misc[0];
-    const int Ur = U - n_static;
-    const int kcn_r = kcn_for(Ur * S, kmax, G);
-    const int Nr = Ur * S * kcn_r;
-    for (int idx = first_from(Ns); idx < Ns + Nr && ok; idx += G) {
-      const int r = idx - Ns;
-      gu_item(idx, n_static + r / (S * kcn_r), (r / kcn_r) % S, r % kcn_r, kcn_r);
-    }
+    gu_range(static_cast<long long>(U - n_static) * S * KB, n_static * S, 1);
     counters_ready();  // (the down phase uses counters too)
     // all activations of this CTA are stored: arrive on the grid barrier of the down phase
     fence_proxy_async_global();
@@ -709,7 +719,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     long long L, QT, q_lo, q_hi;
     d_range(U, L, QT, q_lo, q_hi);
-    auto qlo_of = [&](int b) { return QT * b / G; };
     for (long long q = q_lo; q < q_hi && ok;) {
       const int hs = static_cast<int>(q / L);
       const long long seg_end = (q / L + 1) * L < q_hi ? (q / L + 1) * L : q_hi;
@@ -723,20 +732,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&acce[buf]);
       const int slot = blockIdx.x * kTcMaxSeg + (hs - static_cast<int>(q_lo / L));
       float* pd = p.tc_part_d + static_cast<long long>(slot) * M * 128;
-      for (int t = 0; t < M; ++t) pd[t * 128 + row] = __uint_as_float(v[t]) + __uint_as_float(v[16 + t]);
+#pragma unroll
+      for (int t = 0; t < kMaxM; ++t)
+        if (t < M) pd[t * 128 + row] = __uint_as_float(v[t]) + __uint_as_float(v[16 + t]);
       __threadfence();
       __syncwarp();
       // the CTAs whose ranges meet slice hs, in order; the last to arrive adds their pieces
-      const long long A = static_cast<long long>(hs) * L, B = A + L;
-      int b0 = static_cast<int>(A * G / QT) - 1;
-      if (b0 < 0) b0 = 0;
-      while (b0 > 0 && qlo_of(b0) > A) --b0;
-      int pieces[kMaxPieces];  // slot of each contributing piece, in CTA order (host-checked bound)
-      int np = 0;
-      for (int b = b0; b < G && qlo_of(b) < B && np < kMaxPieces; ++b) {
-        const long long lo = qlo_of(b), hi = qlo_of(b + 1);
-        if (hi > lo && (lo > A ? lo : A) < (hi < B ? hi : B)) pieces[np++] = b * kTcMaxSeg + (hs - static_cast<int>(lo / L));
-      }
+      const long long A = static_cast<long long>(hs) * L;
+      const int np = count_pieces(QT, A, L, G);
       int* cnt = &cnt_d[hs * 4 + g4];
       int last = 0;
       if (lane == 0) last = atomicAdd(cnt, 1) == np - 1;
@@ -744,26 +747,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (last) {
         __threadfence();
         float y[kMaxM];
-        for (int t = 0; t < M; ++t) y[t] = 0.f;
-        const int tot = np * M;
-        for (int c0 = 0; c0 < tot; c0 += 16) {
-          float lv[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int id = c0 + i;
-            if (id < tot) {
-              const int k = id / M, t = id - k * M;
-              lv[i] = ldcg(p.tc_part_d + static_cast<long long>(pieces[k]) * M * 128 + t * 128 + row);
-            }
-          }
+        for (int t = 0; t < kMaxM; ++t) y[t] = 0.f;
+        for_each_piece(QT, A, L, G, 1, 0, kTcMaxSeg, [&](int pslot) {
+          const float* pb = p.tc_part_d + static_cast<long long>(pslot) * M * 128;
+          float lv[kMaxM];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int id = c0 + i;
-            if (id < tot) y[id % M] += lv[i];
-          }
-        }
+          for (int t = 0; t < kMaxM; ++t)
+            if (t < M) lv[t] = ldcg(pb + t * 128 + row);
+#pragma unroll
+          for (int t = 0; t < kMaxM; ++t)
+            if (t < M) y[t] += lv[t];
+        });
         const int col = hs * 128 + row;
-        for (int t = 0; t < M; ++t) {
+#pragma unroll
+        for (int t = 0; t < kMaxM; ++t) {
+          if (t >= M) break;
           float o = y[t];
           if (p.residual != nullptr) o += __uint_as_float(static_cast<uint32_t>(p.residual[t * H + col]) << 16);
           p.out[t * H + col] = f2bf(o);
@@ -798,28 +797,18 @@ struct WsLayout {
 
 static size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 
-static int kmax_of(int H) {
-  int kb = H / 128, k = 1;
-  while (k * 2 <= kb && kb % (k * 2) == 0) k *= 2;
-  return k;
-}
-
 static WsLayout ws_layout(int M, int u_max, int n_static, int u_r_max, int H, int I, int E, int G) {
   WsLayout L{};
-  const int S = I / 128, HS = H / 128, kmax = kmax_of(H);
-  const int kcn_s = n_static > 0 ? kcn_static(n_static * S, kmax, G) : 1;
-  long long items = 0;
-  for (int ur = 0; ur <= u_r_max; ++ur) {
-    const long long n = static_cast<long long>(n_static) * S * kcn_s + static_cast<long long>(ur) * S * kcn_for(ur * S, kmax, G);
-    if (n > items) items = n;
-  }
+  const int S = I / 128, HS = H / 128;
+  (void)n_static;
+  (void)u_r_max;
   size_t o = kWsHeaderBytes;
   L.logits = o;
   o = up256(o + static_cast<size_t>(M) * (E > 0 ? E : 1) * 4);
   L.cnt = o;
   o = up256(o + static_cast<size_t>(u_max * S + HS) * 4 * 4);
   L.part_gu = o;
-  o = up256(o + static_cast<size_t>(items) * 2 * M * 128 * 4);
+  o = up256(o + static_cast<size_t>(G) * 2 * kGuMaxSeg * 2 * M * 128 * 4);
   L.part_d = o;
   o = up256(o + static_cast<size_t>(G) * kTcMaxSeg * M * 128 * 4);
   L.abuf = o;
@@ -880,6 +869,11 @@ int decode_tc_run(decode::Params& p, void* workspace, size_t workspace_bytes, in
   if (workspace_bytes < L.total) return kDecodeTcUnsuitable;
   if ((H / 128 + G - 1) / G + 1 > decode::kTcMaxSeg) return kDecodeTcUnsuitable;
   if ((G + H / 128 - 1) / (H / 128) + 2 > kMaxPieces) return kDecodeTcUnsuitable;
+  {  // gate/up: segments per CTA and pieces per slice within their bounds
+    const long long KB = H / 128, S = I / 128;
+    const long long T_max = static_cast<long long>(u_r_max > n_static ? u_r_max : n_static) * S * KB;
+    if ((T_max + G - 1) / G / KB + 2 > kGuMaxSeg || KB + 2 > kMaxPieces) return kDecodeTcUnsuitable;
+  }
   const int E_alloc = p.router ? p.E : 0;
   const SmemLayout Ls(H, u_max, M, E_alloc, p.router ? p.top_k : 1);
   const size_t smem = Ls.total + 1024;
@@ -894,8 +888,6 @@ int decode_tc_run(decode::Params& p, void* workspace, size_t workspace_bytes, in
   p.tc_abuf = reinterpret_cast<uint16_t*>(ws + L.abuf);
   p.u_max = u_max;
   p.E_alloc = E_alloc;
-  p.tc_kmax = kmax_of(H);
-  p.tc_kcn_s = n_static > 0 ? kcn_static(n_static * (I / 128), p.tc_kmax, G) : 1;
   if (!p.router) p.top_k = 1;  // selection scratch sizing only
 
   CUtensorMap tm_gu, tm_d, tm_ab;

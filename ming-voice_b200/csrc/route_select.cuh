@@ -52,8 +52,10 @@ __device__ __forceinline__ int warp_argmax(const float (&v)[NPER], int E, float&
 // Selection for token m by one warp. `lg` = the token's fp32 logits [E] (global or shared memory).
 // Selection for one token by one warp. `lg` = the token's fp32 logits [E] (global or shared memory), `scr` =
 // E floats of shared scratch owned by this warp (may alias lg). Lane 0 writes sel_out[k] / w_out[k], k < top_k.
-static __device__ __noinline__ void select_core(const SelectCfg& p, const float* lg, float* scr, int* sel_out,
-                                         float* w_out) {
+// (The configuration is taken by value: a reference would keep it in local memory, and every read of it in
+// the unrolled loops below would be a memory access.)
+static __device__ __noinline__ void select_core(const SelectCfg p, const float* lg, float* scr, int* sel_out,
+                                                float* w_out) {
   constexpr int NPER = kMaxE / 32;
   const int lane = threadIdx.x & 31;
   const int E = p.E, K = p.top_k;
