@@ -35,6 +35,7 @@ METRIC = "MoE block us/token @decode M=1 (% HBM peak); prefill tokens/s @1/2/4/8
 UNIT = "us/token"
 LAYERS = 16
 H, I, E, TOPK, IS = 2048, 1408, 64, 6, 2816
+EP_REPLICATED = 8  # experts replicated on every rank in the expert-parallel prefill (the Zipf-hot head)
 
 
 def peaks():
@@ -232,6 +233,50 @@ def prefill_lines(dev, steps, warmup):
             "launches_per_pass": 10, "flops_per_pass": flops}
 
 
+def ep_prefill_lines(dev, world, rank, steps, warmup):
+    """BASELINE C4 with expert parallelism over `world` ranks (NCCL): every rank prefills its own 2043 packed
+    tokens (seed 2 + rank), owns E / world routed experts and keeps the router, norm and shared expert; one
+    all-to-all exchange each way. Weak scaling: tokens/s of the whole job = world * 2043 / max time."""
+    from mingmoe.block import MoeBlock
+    from mingmoe.ep import EPMoeBlock
+    from oracle import moe_oracle as O
+    g = torch.Generator(device=dev).manual_seed(2)  # the same weights on every rank
+    E1 = E + IS // I
+    w_gu = (torch.randn(E1, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w_d = (torch.randn(E1, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    from mingmoe.ep import placement
+    replicated = tuple(range(EP_REPLICATED))  # the Zipf-hot experts (lowest ids) on every rank
+    stacks = placement(E, world, replicated)[2]
+    n_loc = len(stacks[rank])
+    sel = torch.tensor(stacks[rank] + list(range(E, E1)), device=dev)
+    blk = MoeBlock(w_gu.index_select(0, sel).contiguous(), w_d.index_select(0, sel).contiguous(), rw,
+                   torch.ones(H, dtype=torch.bfloat16, device=dev), top_k=TOPK,
+                   shared_ids=tuple(range(n_loc, n_loc + E1 - E)), eps=1e-6, router_bias=O.zipf_bias(E).to(dev))
+    del w_gu, w_d
+    ep = EPMoeBlock(blk, E, replicated=replicated)
+    N = sum(O.PREFILL_LENS)
+    x = O.make_tokens(N, seed=2 + rank).to(dev)
+    for _ in range(warmup):
+        ep.forward(x)
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
+    s_ev.record()
+    for _ in range(steps):
+        ep.forward(x)
+    e_ev.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s_ev.elapsed_time(e_ev) / steps], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    us = t.item() * 1e3
+    flops = O.prefill_flops(N) * world
+    return {"tokens_per_gpu": N, "us_per_pass": round(us, 1), "tokens_per_s": round(world * N / us * 1e6, 0),
+            "tflops": round(flops / us / 1e6, 1),
+            "parallelism": f"ep{world}: experts 0-{EP_REPLICATED - 1} replicated, {E - EP_REPLICATED} round-robin",
+            "exchange": "NCCL all-to-all-v of token rows and weighted outputs", "flops_per_pass": flops}
+
+
 def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -307,13 +352,18 @@ def run_ours(args):
         torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
     e2e_us = t2.item() / args.steps * 1e3 / LAYERS
 
-    pre = prefill_lines(dev, max(3, min(args.steps, 50)), args.warmup) if not args.no_prefill else None
+    pre = None
+    if not args.no_prefill:
+        if world > 1:
+            pre = ep_prefill_lines(dev, world, rank, max(3, min(args.steps, 20)), args.warmup)
+        else:
+            pre = prefill_lines(dev, max(3, min(args.steps, 50)), args.warmup)
     peak, peak_kind = peaks()
     byts = O.decode_bytes(U)  # algorithmic bytes of one block step (M=1)
     achieved = byts / (us_per_block * 1e-6) / 1e9
     out = None
     if rank == 0:
-        cpu_v, cores, sample = cpu_block_time_us()
+        cpu_v, cores, sample = cpu_block_time_us() if world == 1 else (None, None, None)
         out = {
             "metric": METRIC, "value": round(us_per_block / world, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -328,7 +378,8 @@ def run_ours(args):
                          "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
                          "note": f"{byts / 1e6:.1f} MB algorithmic per block / (graph step time / 16); "
                                  f"peak {peak_kind}"},
-            "cpu_baseline": {"value": round(cpu_v, 1), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": ({"value": round(cpu_v, 1), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+                             if world == 1 else None),
             "e2e": {"value": round(e2e_us / world, 3), "unit": UNIT, "h2d_bytes_per_step": H * 2,
                     "d2h_bytes_per_step": H * 2},
             "gpu_launches": LAYERS * args.steps,
@@ -336,10 +387,13 @@ def run_ours(args):
         }
         if pre is not None:
             tf_peak, tf_kind = peaks_tensor()
-            out["prefill"] = {"metric": "prefill tokens/s (BASELINE configs[3], 1 GPU, one block)", **pre,
-                              "roofline": {"bound": "tensor", "achieved": pre["tflops"], "peak": tf_peak,
-                                           "unit": "TFLOP/s", "frac": round(pre["tflops"] / tf_peak, 4),
-                                           "note": f"algorithmic FLOPs / graph pass time; peak {tf_kind}"}}
+            name = ("prefill tokens/s (BASELINE configs[3], 1 GPU, one block)" if world == 1 else
+                    f"prefill tokens/s (BASELINE configs[3] per rank, expert parallel over {world} GPUs, one block)")
+            out["prefill"] = {"metric": name, **pre,
+                              "roofline": {"bound": "tensor", "achieved": pre["tflops"], "peak": tf_peak * world,
+                                           "unit": "TFLOP/s", "frac": round(pre["tflops"] / (tf_peak * world), 4),
+                                           "note": f"algorithmic FLOPs / pass time; peak {tf_kind}"
+                                                   + (f" x {world} GPUs" if world > 1 else "")}}
     if world > 1:
         torch.distributed.barrier()
         del graph

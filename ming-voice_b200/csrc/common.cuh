@@ -204,7 +204,7 @@ static __device__ __noinline__ bool mbar_wait_lazy(uint64_t* bar, uint32_t parit
 // ------------------------------------------------------------------------------------------ bulk copies
 
 // 1-D bulk copy global -> shared (TMA engine), completion counted on `bar` in bytes. `src`, `dst` 16-byte
-// aligned, `bytes` a multiple of 16. No multicast.
+// aligned, `bytes` a multiple of 16. Single destination CTA.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
   asm volatile(

@@ -15,7 +15,7 @@ namespace tc {
 // ---------------------------------------------------------------------------------------------- TMA (tiled)
 
 // 2-D / 3-D tiled loads global -> shared through a tensor map (a __grid_constant__ kernel parameter),
-// completion counted in bytes on `bar`. No multicast. The innermost coordinate x must be a multiple of
+// completion counted in bytes on `bar`; this CTA is the only destination. The innermost coordinate x must be a multiple of
 // 16 bytes / element size (the callers pass multiples of 64 bf16 elements).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(

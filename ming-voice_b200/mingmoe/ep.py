@@ -1,0 +1,150 @@
+"""Expert-parallel (EP) prefill of one MoE block over a torch.distributed process group (NCCL, one rank per GPU).
+
+Placement. Every rank holds the router, the RMSNorm weight and the shared-expert slots (data parallel), the
+`replicated` experts (the hottest ones: their pairs never leave the rank), and a round-robin share of the
+other ("cold") experts: cold expert number c (in id order) lives on rank c % world. With BASELINE's Zipf router
+bias six experts take ~80 % of all routed pairs, so sharding them would serialise the step on their owners;
+replicating them costs 17 MB per expert of the 180 GB on each GPU.
+
+A prefill step on a rank's own packed tokens:
+  1. RMSNorm and routing locally (mv_rmsnorm, mv_route);
+  2. the (token, routed expert) pairs sorted by owner rank (stable, so every rank sends in token order);
+     pair counts exchanged with one all-to-all, then the token rows (bf16 [H]) and their metadata (slot of the
+     expert on its owner, routing weight) with all-to-all-v -- the one exchange step of the block (a
+     replicated expert's pairs go to the rank itself, i.e. stay local);
+  3. the owner computes weight * expert(row) for every received pair with the tcgen05 grouped GEMM
+     (mv_moe_prefill, one expert per row);
+  4. the weighted outputs travel back (all-to-all-v, the reverse split) and are added at the origin in fp32,
+     together with the shared expert (computed locally) and the residual.
+
+The exchange sizes are data dependent, so a step synchronises the host once (the split sizes); prefill is not
+graph-captured. No kernel reads another GPU's memory: everything remote arrives through NCCL.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import moe
+
+
+def placement(E: int, world: int, replicated=()):
+    """owner[e], slot[e] for every routed expert e: replicated experts -> slot i on every rank (owner -1 =
+    "this rank"); cold experts -> rank c % world, slot n_rep + c // world. Also each rank's stack order."""
+    rep = list(replicated)
+    rset = set(rep)
+    cold = [e for e in range(E) if e not in rset]
+    owner = [-1] * E
+    slot = [0] * E
+    for i, e in enumerate(rep):
+        slot[e] = i
+    for c, e in enumerate(cold):
+        owner[e] = c % world
+        slot[e] = len(rep) + c // world
+    stacks = [rep + [e for c, e in enumerate(cold) if c % world == r] for r in range(world)]
+    return owner, slot, stacks
+
+
+class EPMoeBlock:
+    """One rank's part of an expert-parallel MoE block.
+
+    `block` is this rank's MoeBlock: the FULL router / norm, and stacked weights in the order
+    placement(E, world, replicated)[2][rank] followed by the shared slots (see shard_block_params).
+    `experts_fn(x, ids, wts)` computes weight * expert(x) per row on this rank's stacks (defaults to the CUDA
+    grouped GEMM; the CPU tests pass a reference)."""
+
+    def __init__(self, block, E: int, group=None, replicated=(), experts_fn=None):
+        self.block = block
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.E = E
+        owner, slot, stacks = placement(E, self.world, replicated)
+        self.n_local = len(stacks[self.rank])
+        own = torch.tensor(owner, dtype=torch.long)
+        self.owner = torch.where(own < 0, torch.full_like(own, self.rank), own)
+        self.slot = torch.tensor(slot, dtype=torch.long)
+        self.n_shared = len(block.shared_ids)
+        self.experts_fn = experts_fn or self._experts_cuda
+
+    # ------------------------------------------------------------------------------------------ pieces
+    def _experts_cuda(self, x, ids, wts, residual=None):
+        b = self.block
+        return moe.experts(x, b.w_gu, b.w_d, ids, wts, s_gu=b.s_gu, s_d=b.s_d, residual=residual)
+
+    def dispatch_plan(self, ids):
+        """Sort the routed pairs by owner rank. Returns (order [P] pair indices sorted by owner, counts [world])."""
+        K = self.block.top_k
+        routed = ids[:, :K].reshape(-1).long()
+        if self.owner.device != routed.device:
+            self.owner, self.slot = self.owner.to(routed.device), self.slot.to(routed.device)
+        owner = self.owner[routed]
+        order = torch.sort(owner, stable=True).indices
+        counts = torch.bincount(owner, minlength=self.world)
+        return order, counts
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    # ------------------------------------------------------------------------------------------ forward
+    def forward(self, x):
+        """h + MoE(rms_norm(h)) for this rank's N packed tokens x [N, H] bf16."""
+        b = self.block
+        N, H = x.shape
+        K, dev = b.top_k, x.device
+        if b.norm_w is not None:
+            import fused_ops
+            xn = fused_ops.rms_norm(x, b.norm_w, b.eps)
+        else:
+            xn = x
+        ids, wts, _ = b.route(xn)
+
+        order, counts = self.dispatch_plan(ids)
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        in_splits = counts.tolist()
+        out_splits = recv_counts.tolist()  # (the one host synchronisation of the step)
+        R = sum(out_splits)
+
+        tok = torch.div(order, K, rounding_mode="floor")
+        send_rows = xn.index_select(0, tok)
+        routed = ids[:, :K].reshape(-1).long()
+        send_meta = torch.stack([self.slot[routed[order]].to(torch.float32), wts[:, :K].reshape(-1)[order]], 1)
+        recv_rows = torch.empty(R, H, dtype=xn.dtype, device=dev)
+        recv_meta = torch.empty(R, 2, dtype=torch.float32, device=dev)
+        self._a2a(recv_rows, send_rows, out_splits, in_splits)
+        self._a2a(recv_meta, send_meta, out_splits, in_splits)
+
+        if R > 0:
+            lid = recv_meta[:, 0].round().to(torch.int32).unsqueeze(1)
+            lw = recv_meta[:, 1].contiguous().unsqueeze(1)
+            y_pairs = self.experts_fn(recv_rows, lid, lw)
+        else:
+            y_pairs = torch.empty(0, H, dtype=xn.dtype, device=dev)
+
+        back = torch.empty(order.numel(), H, dtype=y_pairs.dtype, device=dev)
+        self._a2a(back, y_pairs.contiguous(), in_splits, out_splits)
+
+        # shared expert locally (the slots after this rank's routed stacks, weight 1)
+        y = x.to(torch.float32, copy=True)  # (never an alias of the caller's tokens)
+        if self.n_shared:
+            sid = torch.arange(self.n_local, self.n_local + self.n_shared, dtype=torch.int32, device=dev)
+            s_ids = sid.unsqueeze(0).expand(N, -1).contiguous()
+            s_w = torch.ones(N, self.n_shared, dtype=torch.float32, device=dev)
+            y += self.experts_fn(xn, s_ids, s_w).float()
+        y.index_add_(0, tok, back.float())
+        return y.to(x.dtype)
+
+
+def shard_block_params(p: dict, rank: int, world: int, E: int, replicated=()):
+    """This rank's stacked weights from a full parameter dict (oracle.make_block_params layout), in the order
+    placement() gives, followed by the shared slots; shared_ids re-numbered to follow the routed stacks."""
+    _, _, stacks = placement(E, world, replicated)
+    sel = stacks[rank] + list(range(E, p["w_gu"].shape[0]))
+    q = dict(p)
+    for k in ("w_gu", "w_d", "s_gu", "s_d"):
+        if q.get(k) is not None:
+            q[k] = p[k][sel].contiguous()
+    n_loc = len(stacks[rank])
+    q["shared_ids"] = tuple(range(n_loc, n_loc + len(p["shared_ids"])))
+    return q

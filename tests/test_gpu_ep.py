@@ -1,0 +1,61 @@
+"""Expert-parallel prefill on 2 GPUs over NCCL (skipped with fewer than 2 GPUs): each rank's output equals
+the single-GPU block on its own tokens (both through the CUDA kernels)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_REL = 2e-2, 1e-2
+
+
+def _worker(rank, world, port, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "ming-voice_b200")]
+    import torch.distributed as dist
+    from mingmoe.block import MoeBlock
+    from mingmoe.ep import EPMoeBlock, shard_block_params
+    from oracle import moe_oracle as O
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        p = O.make_block_params(seed=7, H=1024, I=512, E=16, I_s=1024)
+        bias = O.zipf_bias(16)
+        loc = shard_block_params(p, rank, world, 16, replicated=(0, 1))
+        blk = MoeBlock.from_params(loc, router_bias=bias)
+        ep = EPMoeBlock(blk, 16, replicated=(0, 1))
+        x = O.make_tokens(300 + 37 * rank, H=1024, seed=rank)
+        y = ep.forward(x.cuda())
+        ref, _, _, _ = O.moe_block(x, p, top_k=6, bias=bias)
+        d = (y.float().cpu() - ref).abs()
+        q.put((rank, d.max().item(), (d.sum() / ref.abs().sum()).item()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_prefill_two_gpus():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=300)
+    for pr in procs:
+        if pr.is_alive():
+            pr.kill()
+    assert all(pr.exitcode == 0 for pr in procs)
+    for _ in range(2):
+        rank, mx, mr = q.get(timeout=5)
+        assert mx <= MAX_ABS and mr <= MEAN_REL, (rank, mx, mr)
