@@ -100,6 +100,17 @@ MV_API int mv_quantize_rows_int8(const void* w, int w_dtype, long long w_stride,
 MV_API int mv_dequant_rows_int8(const int8_t* q, const void* scale, int scale_dtype, long long rows, int K,
                          float* out, void* stream);
 
+/* Small-M linear layer: replaces fastlinear.small_linear's kernel path (fastlinear.py:142-174, kernel
+ * _small_m_linear :20-62). y[m] = bf16( act(norm?(x[m]) @ W^T + bias) [+ residual[m]] ) for M <= 16 rows.
+ * x [M, K] bf16 (row stride x_stride), W [N, K] bf16 (row stride w_stride), bias [N] bf16 or NULL,
+ * residual [M, N] bf16 (row stride residual_stride) or NULL, norm_w [K] bf16 or NULL (RMSNorm prologue with
+ * eps, as mv_rmsnorm), act 0 none / 1 gelu-tanh / 2 silu (on the bf16-rounded pre-activation; with a
+ * residual the activation is rounded to bf16 before the add), y [M, N] bf16 (row stride y_stride).
+ * Requirements: K a multiple of 8, M * K * 2 <= 200 KB, 16-byte aligned x / W / norm_w and row strides. */
+MV_API int mv_small_linear(const void* x, long long x_stride, const void* w, long long w_stride, const void* bias,
+                           const void* residual, long long residual_stride, const void* norm_w, float eps, int act,
+                           void* y, long long y_stride, int M, int N, int K, void* stream);
+
 /* Stacked expert weights in the reference layout (engine.py:150-188, fused_moe.py:3-6):
  * w_gu [E1, 2I, H] (gate rows [0, I), up rows [I, 2I)), w_d [E1, H, I]; inner stride 1; strides in elements.
  * w_dtype MV_BF16 or MV_I8; int8 weights carry per-output-row scales s_gu [E1, 2I] and s_d [E1, H]

@@ -63,6 +63,7 @@ _SIGS = {
     "mv_moe_decode_workspace_bytes_tc": (SZ, [I32, I32, I32, I32, I32]),
     "mv_block_decode_noalloc": (I32, [C.POINTER(Block), P, I32, P, P, P, I32, P, P, P]),
     "mv_moe_align": (I32, [P, I32, I32, I32, I32, P, P, P, P, SZ, P]),
+    "mv_small_linear": (I32, [P, I64, P, I64, P, P, I64, P, F32, I32, P, I64, I32, I32, I32, P]),
     "mv_moe_align_workspace_bytes": (SZ, [I32, I32]),
     "mv_moe_prefill": (I32, [C.POINTER(MoeWeights), P, I64, P, I32, P, I32, I32, P, I64, P, P, SZ, P]),
     "mv_moe_prefill_workspace_bytes": (SZ, [I32, I32, I32, I32, I32]),
