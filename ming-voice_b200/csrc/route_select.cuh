@@ -52,11 +52,47 @@ __device__ __forceinline__ int warp_argmax(const float (&v)[NPER], int E, float&
 // Selection for token m by one warp. `lg` = the token's fp32 logits [E] (global or shared memory).
 // Selection for one token by one warp. `lg` = the token's fp32 logits [E] (global or shared memory), `scr` =
 // E floats of shared scratch owned by this warp (may alias lg). Lane 0 writes sel_out[k] / w_out[k], k < top_k.
-// (The configuration is taken by value: a reference would keep it in local memory, and every read of it in
-// the unrolled loops below would be a memory access.)
-static __device__ __noinline__ void select_core(const SelectCfg p, const float* lg, float* scr, int* sel_out,
-                                                float* w_out) {
-  constexpr int NPER = kMaxE / 32;
+// Order-preserving 32-bit key of a float (larger float -> larger unsigned key; -inf is the smallest finite key).
+__device__ __forceinline__ uint32_t sort_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Arg-max over the warp's E values (lane l holds entries l + 32 j): the largest value, ties to the lower index,
+// with two warp reductions (redux.sync) instead of a shuffle tree.
+template <int NPER>
+__device__ __forceinline__ int warp_argmax_redux(const float (&v)[NPER], int E, float& best_v) {
+  const int lane = threadIdx.x & 31;
+  uint32_t bk = 0u;
+  uint32_t bi = 0xffffffffu;
+#pragma unroll
+  for (int j = 0; j < NPER; ++j) {
+    const int e = lane + 32 * j;
+    if (e < E) {
+      const uint32_t k = sort_key(v[j]);
+      if (k > bk) {  // entries are visited in increasing index: '>' keeps the lower index on ties
+        bk = k;
+        bi = static_cast<uint32_t>(e);
+      }
+    }
+  }
+  const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+  const uint32_t idx = __reduce_min_sync(0xffffffffu, bk == mk ? bi : 0xffffffffu);
+  best_v = key_value(mk);
+  return static_cast<int>(idx);
+}
+
+// Selection for one token by one warp. `lg` = the token's fp32 logits [E] (global or shared memory), `scr` =
+// E floats of shared scratch owned by this warp (may alias lg). Lane 0 writes sel_out[k] / w_out[k], k < top_k.
+// NPER = ceil(E / 32) values per lane. The configuration is taken by value (a reference would keep it in local
+// memory, and every read of it in the unrolled loops would be a memory access).
+template <int NPER>
+static __device__ __noinline__ void select_core_t(const SelectCfg p, const float* lg, float* scr, int* sel_out,
+                                                  float* w_out) {
   const int lane = threadIdx.x & 31;
   const int E = p.E, K = p.top_k;
   float r[NPER];
@@ -100,18 +136,11 @@ static __device__ __noinline__ void select_core(const SelectCfg p, const float* 
     // keep the topk_group best groups (first maximum wins ties)
     unsigned int keep = 0u;
     for (int t = 0; t < p.topk_group; ++t) {
-      float bv = (lane < G && !((keep >> lane) & 1u)) ? gs : -INFINITY;
-      int bi = lane < G && !((keep >> lane) & 1u) ? lane : 0x7fffffff;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if (bi < G) keep |= 1u << bi;
+      const bool live = lane < G && !((keep >> lane) & 1u);
+      const uint32_t k = live ? sort_key(gs) : 0u;
+      const uint32_t mk = __reduce_max_sync(0xffffffffu, k);
+      const uint32_t bi = __reduce_min_sync(0xffffffffu, (live && k == mk) ? static_cast<uint32_t>(lane) : 0xffffffffu);
+      if (bi < static_cast<uint32_t>(G)) keep |= 1u << bi;
     }
 #pragma unroll
     for (int j = 0; j < NPER; ++j) {
@@ -124,7 +153,7 @@ static __device__ __noinline__ void select_core(const SelectCfg p, const float* 
   float my_r = -INFINITY, my_s = 0.f;
   for (int k = 0; k < K; ++k) {
     float bv;
-    const int bi = warp_argmax<NPER>(r, E, bv);
+    const int bi = warp_argmax_redux<NPER>(r, E, bv);
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < NPER; ++j)
@@ -153,6 +182,18 @@ static __device__ __noinline__ void select_core(const SelectCfg p, const float* 
     sel_out[lane] = my_sel;
     w_out[lane] = static_cast<float>(wk);
   }
+}
+
+__device__ __forceinline__ void select_core(const SelectCfg& p, const float* lg, float* scr, int* sel_out,
+                                            float* w_out) {
+  if (p.E <= 64)
+    select_core_t<2>(p, lg, scr, sel_out, w_out);
+  else if (p.E <= 128)
+    select_core_t<4>(p, lg, scr, sel_out, w_out);
+  else if (p.E <= 256)
+    select_core_t<8>(p, lg, scr, sel_out, w_out);
+  else
+    select_core_t<kMaxE / 32>(p, lg, scr, sel_out, w_out);
 }
 
 }  // namespace route
