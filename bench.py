@@ -284,10 +284,11 @@ def run_ours(args):
     from oracle import moe_oracle as O
     LAYERS = args.layers
     blocks = make_stack(dev, LAYERS)
-    x0 = O.make_tokens(1, seed=3).to(dev)
-    bufs = [torch.empty(1, H, dtype=torch.bfloat16, device=dev) for _ in range(LAYERS + 1)]
+    Md = args.decode_m
+    x0 = O.make_tokens(Md, seed=3).to(dev)
+    bufs = [torch.empty(Md, H, dtype=torch.bfloat16, device=dev) for _ in range(LAYERS + 1)]
     bufs[0].copy_(x0)
-    ids = torch.empty(1, TOPK + 2, dtype=torch.int32, device=dev)
+    ids = torch.empty(Md, TOPK + 2, dtype=torch.int32, device=dev)
 
     def step():
         for layer, blk in enumerate(blocks):
@@ -331,9 +332,9 @@ def run_ours(args):
     us_per_block = ms_per_step * 1e3 / LAYERS
 
     # end to end through the public API: pinned host token in, result out, every step (eager calls)
-    h_in = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
+    h_in = torch.empty(Md, H, dtype=torch.bfloat16).pin_memory()
     h_in.copy_(x0.cpu())
-    h_out = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
+    h_out = torch.empty(Md, H, dtype=torch.bfloat16).pin_memory()
     for _ in range(args.warmup):
         bufs[0].copy_(h_in, non_blocking=True)
         step()
@@ -359,18 +360,19 @@ def run_ours(args):
         else:
             pre = prefill_lines(dev, max(3, min(args.steps, 50)), args.warmup)
     peak, peak_kind = peaks()
-    byts = O.decode_bytes(U)  # algorithmic bytes of one block step (M=1)
+    byts = O.decode_bytes(U, M=Md)  # algorithmic bytes of one block step
     achieved = byts / (us_per_block * 1e-6) / 1e9
     out = None
     if rank == 0:
         cpu_v, cores, sample = cpu_block_time_us() if world == 1 else (None, None, None)
         out = {
-            "metric": METRIC, "value": round(us_per_block / world, 3), "unit": UNIT, "n_gpus": world,
+            "metric": METRIC, "value": round(us_per_block / Md / world, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights generated on the device; N(0,1) token)",
-            "config": {"workload": "decode M=1 through a 16-layer chain of MoE blocks (BASELINE configs[1] at M=1, "
-                                   "run as configs[4](a): one CUDA graph per step, one kernel per block)",
+            "config": {"workload": f"decode M={Md} through a 16-layer chain of MoE blocks (BASELINE configs[1] at "
+                                   f"M={Md}, run as configs[4](a): one CUDA graph per step, one kernel per block)",
+                       "tokens_per_step": Md,
                        "layers": LAYERS, "H": H, "I": I, "E": E, "top_k": TOPK, "shared_I": IS,
                        "routed_experts_hit": U, "parallelism": f"replicas x{world}",
                        "l2": "weights per step (16 x 139 MB) exceed L2; no flush"},
@@ -380,8 +382,8 @@ def run_ours(args):
                                  f"peak {peak_kind}"},
             "cpu_baseline": ({"value": round(cpu_v, 1), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
                              if world == 1 else None),
-            "e2e": {"value": round(e2e_us / world, 3), "unit": UNIT, "h2d_bytes_per_step": H * 2,
-                    "d2h_bytes_per_step": H * 2},
+            "e2e": {"value": round(e2e_us / Md / world, 3), "unit": UNIT, "h2d_bytes_per_step": H * 2 * Md,
+                    "d2h_bytes_per_step": H * 2 * Md},
             "gpu_launches": LAYERS * args.steps,
             "clocks": clk.summary(),
         }
@@ -410,6 +412,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="blocks in the chain (1 = the small profiling case)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) measurement")
+    ap.add_argument("--decode-m", type=int, default=1, choices=range(1, 17), metavar="M",
+                    help="tokens per decode step (1 = the headline; 2..16 = the other configs[1] points)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the prefill measurement (the profiling case for the grouped GEMMs)")
     args = ap.parse_args()
