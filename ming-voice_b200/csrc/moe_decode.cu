@@ -723,9 +723,10 @@ using decode::Params;
 
 // Token count from which the tensor-core kernel (moe_decode_tc.cu) takes over: below it the step is pure
 // weight streaming with little arithmetic, and this CUDA-core kernel's row-granular split (no split-K
-// partial sums to combine across CTAs) measured faster; from 4 tokens on the tensor cores win (3x at 8-16).
+// partial sums to combine across CTAs) measured faster at M = 1; from 2 tokens on the tensor cores win
+// (16-layer graph, per token: M = 2 45 vs 55 us, M = 4 28 vs 40 us; 3x at 16).
 // MINGMOE_DECODE_PATH=classic / =tc forces either kernel.
-constexpr int kTcMinM = 4;
+constexpr int kTcMinM = 2;
 
 // Geometry, validation and the cooperative launch; shared by mv_moe_decode and mv_block_decode.
 int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t workspace_bytes, int nk_pairs,
@@ -781,7 +782,7 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
   p.I = I;
   p.s_bf16 = w->s_dtype == MV_BF16;
   p.ws = static_cast<WsHeader*>(workspace);
-  if (!int8) {  // the tensor-core kernel when the shapes and the workspace suit it (M >= 4; see kTcMinM)
+  if (!int8) {  // the tensor-core kernel when the shapes and the workspace suit it (M >= kTcMinM)
     const char* path = getenv("MINGMOE_DECODE_PATH");
     const bool force_tc = path != nullptr && path[0] == 't';
     if ((path == nullptr || path[0] != 'c') && (M >= kTcMinM || force_tc)) {

@@ -778,7 +778,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
-  if (tid == 0) {  // the last CTA resets the grid-barrier counters for the next call
+  // (an epilogue thread, not thread 0: thread 0 is the TMA producer, and its fence would wait on its bulk copies)
+  if (tid == 64) {  // the last CTA resets the grid-barrier counters for the next call
     __threadfence();
     if (atomicAdd(&p.ws->counter, 1u) == static_cast<unsigned int>(G - 1)) {
       atomicExch(&p.ws->bar1, 0u);
