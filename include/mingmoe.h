@@ -166,13 +166,15 @@ MV_API size_t mv_moe_align_workspace_bytes(int P, int E1);
  * x [N, H] bf16 (row stride x_stride), ids [N, NK] i32/i64, wts [N, NK] f32, residual [N, H] bf16 (row stride
  * residual_stride) or NULL, out [N, H] bf16 contiguous. Gate/up accumulate in fp32; the activation is rounded
  * to bf16 once (the tensor-core operand of the down projection); the per-pair outputs are weighted and summed
- * in fp32 (reduction order not fixed). Weights bf16 (int8 prefill: see mv_moe_decode over chunks).
- * workspace: mv_moe_prefill_workspace_bytes(N, NK, H, I, E1) bytes, 256-byte aligned, header zeroed.
+ * in fp32 (reduction order not fixed). Weights bf16, or int8 with row scales: the experts in use are widened to
+ * bf16 (exact) in the workspace and the scales multiply the fp32 products, as the reference's int8 kernels do.
+ * workspace: mv_moe_prefill_workspace_bytes(N, NK, H, I, E1, w_dtype) bytes, 256-byte aligned, header zeroed
+ * (int8 adds bf16 copies of the stacks: E1 * 3 * I * H * 2 bytes).
  * Requirements: H a multiple of 256, I a multiple of 128, E1 <= 512, 16-byte aligned pointers/strides. */
 MV_API int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids, int ids_dtype,
                           const float* wts, int N, int NK, const void* residual, long long residual_stride, void* out,
                           void* workspace, size_t workspace_bytes, void* stream);
-MV_API size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1);
+MV_API size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1, int w_dtype);
 
 /* Workspace for the fastest decode path (the tensor-core kernel, bf16 weights, H and I multiples of 128,
  * H <= 2048): larger than mv_moe_decode_workspace_bytes, which is the minimum (with the minimum the CUDA-core

@@ -219,6 +219,44 @@ __global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__
   }
 }
 
+// ------------------------------------------------------------------------------------------------ int8 weights
+
+// int8 expert rows -> bf16 rows (exact: |q| <= 127), for the experts the blocks in use refer to; the scales are
+// applied to the fp32 products in the GEMM epilogues, as the reference's int8 kernels do (fused_moe.py:115-121).
+// Grid: (row groups, E1); a CTA of an expert no block uses returns at once.
+__global__ void __launch_bounds__(256) widen_experts_kernel(const int8_t* __restrict__ q, long long q_se, long long q_sr,
+                                                            int rows, int K, const int* __restrict__ bexp,
+                                                            const int* __restrict__ nb_used, uint16_t* __restrict__ out) {
+  const int e = blockIdx.y;
+  __shared__ int used;
+  if (threadIdx.x == 0) used = 0;
+  __syncthreads();
+  const int nb = *nb_used;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x)
+    if (bexp[b] == e) used = 1;
+  __syncthreads();
+  if (!used) return;
+  const int nv = K / 16;  // 16 int8 per 16-byte load
+  const int r0 = blockIdx.x * 16;
+  for (int i = threadIdx.x; i < 16 * nv; i += blockDim.x) {
+    const int r = r0 + i / nv, v = i % nv;
+    if (r >= rows) break;
+    const uint4 w = *reinterpret_cast<const uint4*>(q + e * q_se + r * q_sr + v * 16);
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float f0, f1, f2, f3;
+      i8x4_to_f32(ww[k], f0, f1, f2, f3);
+      o[2 * k] = static_cast<uint32_t>(f2bf(f0)) | (static_cast<uint32_t>(f2bf(f1)) << 16);
+      o[2 * k + 1] = static_cast<uint32_t>(f2bf(f2)) | (static_cast<uint32_t>(f2bf(f3)) << 16);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<long long>(e) * rows + r) * K + v * 16);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ GEMMs
 
 struct GemmArgs {
@@ -231,8 +269,16 @@ struct GemmArgs {
   uint16_t* a_out;     // gate/up: [rows, I] bf16
   float* y32;          // down: [N, H] fp32 accumulator
   const float* wts;    // down: [P] routing weights
+  const void* scale;   // int8 weights: per-row scales of the B operand (s_gu [E1, 2I] / s_d [E1, H]), else NULL
+  long long scale_se;  // expert stride of `scale` (elements)
+  int scale_bf16;      // 1: bf16 scales, 0: f32
   WsHeader* ws;
 };
+
+__device__ __forceinline__ float ld_scale(const void* base, long long i, int bf16) {
+  return bf16 ? __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t*>(base)[i]) << 16)
+              : static_cast<const float*>(base)[i];
+}
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
 
@@ -373,6 +419,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           tc::tmem_ld32(taddr + c * 32, gr);
           tc::tmem_ld32(taddr + kGuHalf + c * 32, ur);
           tc::tmem_ld_wait();
+          if (g.scale != nullptr) {  // int8: the fp32 dot product times the weight row's scale (as the reference)
+            const long long sb = static_cast<long long>(g.bexp[blk]) * g.scale_se + nt * kGuHalf + c * 32;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              gr[i] = __float_as_uint(__uint_as_float(gr[i]) * ld_scale(g.scale, sb + i, g.scale_bf16));
+              ur[i] = __float_as_uint(__uint_as_float(ur[i]) * ld_scale(g.scale, sb + g.I + i, g.scale_bf16));
+            }
+          }
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -398,6 +452,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           uint32_t v[32];
           tc::tmem_ld32(taddr + c * 32, v);
           tc::tmem_ld_wait();
+          if (live && g.scale != nullptr) {
+            const long long sb = static_cast<long long>(g.bexp[blk]) * g.scale_se + nt * kDownN + c * 32;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * ld_scale(g.scale, sb + i, g.scale_bf16));
+          }
           if (live) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
@@ -423,12 +482,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 struct Layout {
   int P, nb_max;
   long long rows;
-  size_t off_nb, off_align, off_sorted, off_bexp, off_xs, off_a, off_y32, total;
+  size_t off_nb, off_align, off_sorted, off_bexp, off_xs, off_a, off_y32, off_wgu, off_wd, total;
 };
 
 static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-static Layout layout(int N, int NK, int H, int I, int E1) {
+static Layout layout(int N, int NK, int H, int I, int E1, bool int8) {
   Layout L{};
   L.P = N * NK;
   L.nb_max = (L.P + E1 * (kBM - 1) + kBM - 1) / kBM;
@@ -448,6 +507,13 @@ static Layout layout(int N, int NK, int H, int I, int E1) {
   o = up(o + static_cast<size_t>(L.rows) * I * 2, 256);
   L.off_y32 = o;
   o = up(o + static_cast<size_t>(N) * H * 4, 256);
+  L.off_wgu = L.off_wd = 0;
+  if (int8) {  // bf16 copies of the int8 experts in use (same stacked layout, contiguous)
+    L.off_wgu = o;
+    o = up(o + static_cast<size_t>(E1) * 2 * I * H * 2, 256);
+    L.off_wd = o;
+    o = up(o + static_cast<size_t>(E1) * H * I * 2, 256);
+  }
   L.total = o;
   return L;
 }
@@ -529,9 +595,9 @@ extern "C" size_t mv_moe_align_workspace_bytes(int P, int E1) {
   return kWsHeaderBytes + align_scratch_bytes(P > 0 ? P : 0, E1 > 0 ? E1 : 1);
 }
 
-extern "C" size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1) {
+extern "C" size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1, int w_dtype) {
   if (N < 0 || NK < 1 || H < 1 || I < 1 || E1 < 1) return 0;
-  return layout(N, NK, H, I, E1).total;
+  return layout(N, NK, H, I, E1, w_dtype == MV_I8).total;
 }
 
 extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids,
@@ -541,7 +607,10 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   if (w == nullptr || (N > 0 && (x == nullptr || ids == nullptr || wts == nullptr || out == nullptr)))
     return fail(MV_ERR_INVALID, "mv_moe_prefill: null pointer argument");
   if (ids_dtype != MV_I32 && ids_dtype != MV_I64) return fail(MV_ERR_INVALID, "mv_moe_prefill: ids must be i32 or i64");
-  if (w->w_dtype != MV_BF16) return fail(MV_ERR_UNSUPPORTED, "mv_moe_prefill: tensor-core path takes bf16 weights");
+  const bool int8 = w->w_dtype == MV_I8;
+  if (!int8 && w->w_dtype != MV_BF16) return fail(MV_ERR_UNSUPPORTED, "mv_moe_prefill: weights must be bf16 or int8");
+  if (int8 && (w->s_gu == nullptr || w->s_d == nullptr || (w->s_dtype != MV_F32 && w->s_dtype != MV_BF16)))
+    return fail(MV_ERR_INVALID, "mv_moe_prefill: int8 weights need f32/bf16 scales s_gu and s_d");
   const int H = w->H, I = w->I, E1 = w->E1;
   if (N < 0 || NK < 1 || NK > 64) return fail(MV_ERR_INVALID, "mv_moe_prefill: bad N=%d / NK=%d", N, NK);
   if (H % kDownN != 0 || I % kGuHalf != 0 || H > 65536 || I > 65536)
@@ -549,13 +618,14 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   if (E1 < 1 || E1 > kAlignMaxE1) return fail(MV_ERR_INVALID, "mv_moe_prefill: E1=%d outside [1, %d]", E1, kAlignMaxE1);
   if (static_cast<long long>(N) * NK > 0x7fffffffLL / 2) return fail(MV_ERR_INVALID, "mv_moe_prefill: too many pairs");
   if (N == 0) return MV_OK;
+  const int esz = int8 ? 1 : 2;
   if (!aligned16(w->w_gu) || !aligned16(w->w_d) || !aligned16(x) || !aligned16(out) ||
       (residual != nullptr && (!aligned16(residual) || (residual_stride * 2) % 16)) || (x_stride * 2) % 16 ||
-      (w->gu_sr * 2) % 16 || (w->gu_se * 2) % 16 || (w->d_sr * 2) % 16 || (w->d_se * 2) % 16)
+      (w->gu_sr * esz) % 16 || (w->gu_se * esz) % 16 || (w->d_sr * esz) % 16 || (w->d_se * esz) % 16)
     return fail(MV_ERR_ALIGN, "mv_moe_prefill: pointers and row strides must be 16-byte aligned");
   if (x_stride < H || (residual != nullptr && residual_stride < H))
     return fail(MV_ERR_INVALID, "mv_moe_prefill: row stride shorter than H");
-  const Layout L = layout(N, NK, H, I, E1);
+  const Layout L = layout(N, NK, H, I, E1, int8);
   if (workspace == nullptr || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return fail(MV_ERR_WORKSPACE, "mv_moe_prefill: 256-byte aligned workspace of %zu bytes needed", L.total);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -567,6 +637,13 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   uint16_t* abuf = reinterpret_cast<uint16_t*>(ws + L.off_a);
   float* y32 = reinterpret_cast<float*>(ws + L.off_y32);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // int8: the GEMMs read bf16 copies of the experts in use (exact), contiguous in the workspace
+  uint16_t* wgu16 = int8 ? reinterpret_cast<uint16_t*>(ws + L.off_wgu) : nullptr;
+  uint16_t* wd16 = int8 ? reinterpret_cast<uint16_t*>(ws + L.off_wd) : nullptr;
+  const void* gu_base = int8 ? static_cast<const void*>(wgu16) : w->w_gu;
+  const void* d_base = int8 ? static_cast<const void*>(wd16) : w->w_d;
+  const long long gu_sr = int8 ? H : w->gu_sr, gu_se = int8 ? 2LL * I * H : w->gu_se;
+  const long long d_sr = int8 ? I : w->d_sr, d_se = int8 ? static_cast<long long>(H) * I : w->d_se;
 
   CUtensorMap tm_xs, tm_wgu, tm_a, tm_wd;
   int rc;
@@ -578,9 +655,9 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   }
   {
     const uint64_t d[3] = {static_cast<uint64_t>(H), static_cast<uint64_t>(2 * I), static_cast<uint64_t>(E1)};
-    const uint64_t s[2] = {static_cast<uint64_t>(w->gu_sr) * 2, static_cast<uint64_t>(w->gu_se) * 2};
+    const uint64_t s[2] = {static_cast<uint64_t>(gu_sr) * 2, static_cast<uint64_t>(gu_se) * 2};
     const uint32_t b[3] = {kBK, kGuHalf, 1};
-    if ((rc = make_tmap(&tm_wgu, w->w_gu, 3, d, s, b, "w_gu")) != MV_OK) return rc;
+    if ((rc = make_tmap(&tm_wgu, gu_base, 3, d, s, b, "w_gu")) != MV_OK) return rc;
   }
   {
     const uint64_t d[2] = {static_cast<uint64_t>(I), static_cast<uint64_t>(L.rows)};
@@ -590,9 +667,9 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   }
   {
     const uint64_t d[3] = {static_cast<uint64_t>(I), static_cast<uint64_t>(H), static_cast<uint64_t>(E1)};
-    const uint64_t s[2] = {static_cast<uint64_t>(w->d_sr) * 2, static_cast<uint64_t>(w->d_se) * 2};
+    const uint64_t s[2] = {static_cast<uint64_t>(d_sr) * 2, static_cast<uint64_t>(d_se) * 2};
     const uint32_t b[3] = {kBK, kDownN, 1};
-    if ((rc = make_tmap(&tm_wd, w->w_d, 3, d, s, b, "w_d")) != MV_OK) return rc;
+    if ((rc = make_tmap(&tm_wd, d_base, 3, d, s, b, "w_d")) != MV_OK) return rc;
   }
 
   if ((rc = launch_align(ids, ids_dtype, L.P, E1, kBM, L.nb_max, sorted, bexp, nb_used,
@@ -603,6 +680,13 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
                                        static_cast<const uint16_t*>(residual), residual_stride, y32, N);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "gather launch");
+  if (int8) {
+    widen_experts_kernel<<<dim3((2 * I + 15) / 16, E1), 256, 0, st>>>(static_cast<const int8_t*>(w->w_gu), w->gu_se,
+                                                                     w->gu_sr, 2 * I, H, bexp, nb_used, wgu16);
+    widen_experts_kernel<<<dim3((H + 15) / 16, E1), 256, 0, st>>>(static_cast<const int8_t*>(w->w_d), w->d_se, w->d_sr,
+                                                                 H, I, bexp, nb_used, wd16);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "int8 widening launch");
+  }
 
   GemmArgs ga{};
   ga.sorted = sorted;
@@ -622,10 +706,15 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm)");
   ga.n_tiles = I / kGuHalf;
   ga.k_steps = H / kBK;
+  ga.scale = int8 ? w->s_gu : nullptr;
+  ga.scale_se = w->sgu_se;
+  ga.scale_bf16 = w->s_dtype == MV_BF16;
   gemm_kernel<0><<<G, kThreads, kGemmSmem, st>>>(tm_xs, tm_wgu, ga);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "gate/up GEMM launch");
   ga.n_tiles = H / kDownN;
   ga.k_steps = I / kBK;
+  ga.scale = int8 ? w->s_d : nullptr;
+  ga.scale_se = w->sd_se;
   gemm_kernel<1><<<G, kThreads, kGemmSmem, st>>>(tm_a, tm_wd, ga);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "down GEMM launch");
   const long long n4 = static_cast<long long>(N) * H / 4;

@@ -66,7 +66,7 @@ _SIGS = {
     "mv_small_linear": (I32, [P, I64, P, I64, P, P, I64, P, F32, I32, P, I64, I32, I32, I32, P]),
     "mv_moe_align_workspace_bytes": (SZ, [I32, I32]),
     "mv_moe_prefill": (I32, [C.POINTER(MoeWeights), P, I64, P, I32, P, I32, I32, P, I64, P, P, SZ, P]),
-    "mv_moe_prefill_workspace_bytes": (SZ, [I32, I32, I32, I32, I32]),
+    "mv_moe_prefill_workspace_bytes": (SZ, [I32, I32, I32, I32, I32, I32]),
 }
 
 _lib = None

@@ -1,7 +1,7 @@
 """Multi-token (prefill) expert path: expert-sorted grouped GEMMs on the tensor cores (mv_moe_prefill).
 
-bf16 weights take the tcgen05 path. int8 weights still go through the decode kernel 16 tokens at a time
-(a GPU path with the int8 numerics of fused_moe.py:27-33; not a fallback to PyTorch)."""
+bf16 and int8 weights both take the tcgen05 path (int8: the experts in use are widened to bf16 exactly and the
+row scales multiply the fp32 products, the reference's int8 numerics, fused_moe.py:115-121)."""
 from __future__ import annotations
 
 import ctypes as C
@@ -32,12 +32,6 @@ def align(ids: torch.Tensor, E1: int, BM: int):
 def experts(x, w_gu, w_d, ids, wts, s_gu=None, s_d=None, out=None, residual=None):
     N, H = x.shape
     y = torch.empty(N, H, dtype=torch.bfloat16, device=x.device) if out is None else out
-    if w_gu.dtype == torch.int8:
-        for n0 in range(0, N, moe.DECODE_MAX_M):
-            n1 = min(N, n0 + moe.DECODE_MAX_M)
-            moe.decode(x[n0:n1], w_gu, w_d, ids[n0:n1], wts[n0:n1], out=y[n0:n1], s_gu=s_gu, s_d=s_d,
-                       residual=None if residual is None else residual[n0:n1])
-        return y
     L.require_cuda(x)
     if x.dtype != torch.bfloat16:
         raise TypeError("prefill: x must be bf16")
@@ -47,7 +41,7 @@ def experts(x, w_gu, w_d, ids, wts, s_gu=None, s_d=None, out=None, residual=None
     NK = ids2.shape[1]
     wst = moe.weights_struct(w_gu, w_d, s_gu, s_d)
     E1, I = w_gu.shape[0], w_gu.shape[1] // 2
-    nbytes = L.lib().mv_moe_prefill_workspace_bytes(N, NK, H, I, E1)
+    nbytes = L.lib().mv_moe_prefill_workspace_bytes(N, NK, H, I, E1, L.dt(w_gu))
     ws = L.workspace("prefill", nbytes, x.device)
     r = residual
     if r is not None and r.stride(1) != 1:

@@ -133,3 +133,38 @@ def test_prefill_bad_id_flagged(base_params, base_params_gpu):
     close(got, ref)
     errs = L.all_workspace_errors(clear=True)
     assert any(c == 2 for c, _ in errs.values())
+
+
+@pytest.fixture(scope="module")
+def int8_params():
+    return O.make_block_params(seed=1, int8=True)
+
+
+@pytest.mark.parametrize("N", [17, 300])
+def test_prefill_experts_int8(int8_params, N):
+    """BASELINE C3 weights (int8, bf16 scales) through the tcgen05 prefill: widened exactly, scaled in fp32."""
+    p = int8_params
+    pg = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in p.items()}
+    x = O.make_tokens(N, seed=N + 1)
+    xn = O.rms_norm(x, p["norm_w"], p["eps"])
+    ids, wts, _ = O.route_softmax(xn, p["router_w"], top_k=6, shared_ids=p["shared_ids"], w_scale=p["router_s"])
+    ref = O.moe_experts(xn, p["w_gu"], p["w_d"], ids, wts, s_gu=p["s_gu"], s_d=p["s_d"])
+    got = prefill.experts(xn.cuda(), pg["w_gu"], pg["w_d"], ids.cuda(), wts.cuda(), s_gu=pg["s_gu"], s_d=pg["s_d"])
+    close(got, ref)
+    no_device_errors()
+
+
+def test_prefill_block_int8_reference_model_fp32_scales():
+    """ming-voice's own layout: H=1536, I=512, 128 experts + shared slot, fp32 row scales, sigmoid-group router."""
+    from mingmoe.block import MoeBlock
+    g = torch.Generator().manual_seed(21)
+    E, H, I = 128, 1536, 512
+    p = O.make_block_params(seed=21, H=H, I=I, E=E, I_s=I, int8=True, scale_dtype=torch.float32)
+    # ming-voice keeps an fp32 copy of the gate (engine.py:324) next to int8 experts
+    p["router_w"] = O.dequant_rows_int8(p["router_w"], p.pop("router_s"))
+    p.update(router_bias=torch.randn(E, generator=g) * 0.05, n_group=8, topk_group=4, scale=2.5)
+    blk = MoeBlock.from_params(p, route_mode="sigmoid_group", top_k=8, router_bias=p["router_bias"])
+    x = O.make_tokens(150, H=H, seed=21)
+    y_ref, _, _, _ = O.moe_block(x, p, top_k=8, router="sigmoid_group")
+    close(blk.prefill(x.cuda()), y_ref)
+    no_device_errors()
