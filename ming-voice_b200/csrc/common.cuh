@@ -214,6 +214,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Bulk prefetch of global memory into L2 (no destination, nothing to wait for). `src` 16-byte aligned, `bytes` a
+// multiple of 16. Used to start small latency-critical reads (norm weights) before the weight stream fills the
+// memory queues.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -118,42 +118,35 @@ __device__ __forceinline__ float router_w(const Params& p, long long e, int h) {
   return dequant(static_cast<float>(static_cast<const int8_t*>(p.rw)[i]), s);
 }
 
-// Expert table from (expert, weight) pairs, by ONE warp, for at most 32 pairs: lane j holds pair j; first
-// occurrences, ranks and token positions come from fully unrolled shuffle loops (no serial dependence).
+// Expert table from (expert, weight) pairs, by ONE warp, for at most 32 pairs: lane j holds pair j. Lanes with
+// the same expert (and the same expert and token) are found with match.any, so first occurrences, token
+// positions and counts are ballot / popc arithmetic; the rank of an expert counts the distinct smaller ids, and
+// duplicate (expert, token) weights are summed in pair order.
 template <int MT>
 __device__ void table_warp(const int* pr_e, const float* pr_w, int npairs, int kp, int E1, int n_static, int static_id,
                            int M, int* e_id, int* e_ntok, int* e_tok, float* e_w, int* e_pbase, int* misc, WsHeader* ws) {
+  constexpr unsigned int kFull = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  const int j = lane;
-  const int e = j < npairs ? pr_e[j] : -1;
-  const float wj = j < npairs ? pr_w[j] : 0.f;
-  const int mj = j / kp;
-  const bool valid = j < npairs && e >= 0 && e < E1;
-  bool first = valid, newtok = valid;
+  const bool in = lane < npairs;
+  const int e = in ? pr_e[lane] : -1;
+  const int mj = in ? lane / kp : 0;
+  const bool valid = in && e >= 0 && e < E1;
+  const unsigned int lt = (1u << lane) - 1u;
+  // invalid lanes get keys no other lane has (negative); valid keys are >= 0 (e < kMaxE1, mj < 32)
+  const unsigned int same_e = __match_any_sync(kFull, valid ? e : -2 - lane);
+  const unsigned int same_em = __match_any_sync(kFull, valid ? e * 32 + mj : -2 - lane);
+  const bool first = valid && (same_e & lt) == 0u;
+  const bool newtok = valid && (same_em & lt) == 0u;
+  const unsigned int fmask = __ballot_sync(kFull, first);
+  const unsigned int nmask = __ballot_sync(kFull, newtok);
+  int rank = n_static;
+  for (unsigned int b = fmask; b != 0u; b &= b - 1u)
+    if (pr_e[__ffs(b) - 1] < e) ++rank;
   float wsum = 0.f;
-#pragma unroll
-  for (int k = 0; k < 32; ++k) {
-    const int ek = __shfl_sync(0xffffffffu, e, k);
-    const float wk = __shfl_sync(0xffffffffu, wj, k);
-    const bool vk = k < npairs && ek >= 0 && ek < E1;
-    const bool same = vk && ek == e && (k / kp) == mj;
-    if (vk && k < j && ek == e) first = false;
-    if (same && k < j) newtok = false;
-    if (same) wsum += wk;
-  }
-  int rank = n_static, pos = 0, ntok = 0;
-#pragma unroll
-  for (int k = 0; k < 32; ++k) {
-    const int ek = __shfl_sync(0xffffffffu, e, k);
-    const bool fk = __shfl_sync(0xffffffffu, first, k);
-    const bool nk = __shfl_sync(0xffffffffu, newtok, k);
-    if (fk && valid && ek < e) ++rank;
-    if (nk && valid && ek == e) {
-      if (k < j) ++pos;
-      ++ntok;
-    }
-  }
-  const int nfirst = __popc(__ballot_sync(0xffffffffu, first));
+  if (newtok)
+    for (unsigned int b = same_em; b != 0u; b &= b - 1u) wsum += pr_w[__ffs(b) - 1];
+  const int pos = __popc(nmask & same_e & lt);
+  const int ntok = __popc(nmask & same_e);
   for (int u = lane; u < n_static; u += 32) {
     e_id[u] = static_id + u;
     e_ntok[u] = M;
@@ -170,10 +163,10 @@ __device__ void table_warp(const int* pr_e, const float* pr_w, int npairs, int k
     e_tok[rank * MT + pos] = mj;
     e_w[rank * MT + pos] = wsum;
   }
-  if (newtok && pos >= MT) raise_error(ws, kErrOverflow, static_cast<unsigned int>(j));
+  if (newtok && pos >= MT) raise_error(ws, kErrOverflow, static_cast<unsigned int>(lane));
   __syncwarp();
   if (lane == 0) {
-    const int Ut = n_static + nfirst;
+    const int Ut = n_static + __popc(fmask);
     int pb = 0;
     for (int u = 0; u < Ut; ++u) {
       e_pbase[u] = pb;

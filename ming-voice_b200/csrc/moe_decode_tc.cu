@@ -63,7 +63,7 @@ struct SmemLayout {
     const uint32_t xbb = static_cast<uint32_t>(H) * 32u;  // 16 token rows x H bf16
     o += ((xbb > static_cast<uint32_t>(kStages * kBTile) ? xbb : kStages * kBTile) + 1023u) & ~1023u;
     bars = o;
-    o += (2 * kStages + 6) * 8;
+    o += (2 * kStages + 7) * 8;
     tmem = o;
     o += 16;
     misc = o;
@@ -137,20 +137,28 @@ __device__ __forceinline__ float ldcg(const float* p) {
 
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// fp64 router logits of one expert row against the (swizzled) normalised tokens; one warp. All of the lane's
-// row chunks are loaded before any is used (the row reads then cost one memory latency, not H / 256).
+// The router warps read their expert rows at kernel entry, into registers (16-byte chunks c = lane + 32 i of
+// the row), and compute the logits once the tokens are normalised.
+constexpr int kRouterChunks = kMaxH * 4 / 16 / 32;  // chunks per lane of an fp32 row at H = kMaxH
+
+__device__ __forceinline__ void router_row_load(const void* w_row, int row_bytes, uint4 (&buf)[kRouterChunks]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < kRouterChunks; ++i) {
+    const int c = lane + 32 * i;
+    if (c * 16 < row_bytes) buf[i] = ld_nc_v4(static_cast<const uint8_t*>(w_row) + static_cast<size_t>(c) * 16);
+  }
+}
+
+// fp64 router logits of one expert row (loaded by router_row_load) against the (swizzled) normalised tokens;
+// one warp.
 template <int DT>
-__device__ void router_logits_sw(const void* w_row, float sc, const uint8_t* xb, int H, int M, double (&acc)[kMaxM]) {
+__device__ void router_logits_sw(const uint4 (&buf)[kRouterChunks], float sc, const uint8_t* xb, int H, int M,
+                                 double (&acc)[kMaxM]) {
   const int lane = threadIdx.x & 31;
   constexpr int per = DT == MV_F32 ? 4 : (DT == MV_BF16 ? 8 : 16);
   constexpr int kMaxCh = kMaxH / per / 32;  // chunks per lane at H = kMaxH
   const int nch = H / per;
-  uint4 buf[kMaxCh];
-#pragma unroll
-  for (int i = 0; i < kMaxCh; ++i) {
-    const int c = lane + 32 * i;
-    if (c < nch) buf[i] = ld_nc_v4(static_cast<const uint8_t*>(w_row) + static_cast<size_t>(c) * 16);
-  }
 #pragma unroll
   for (int i = 0; i < kMaxCh; ++i) {
     const int c = lane + 32 * i;
@@ -206,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acce = accf + 2;
   uint64_t* tbl = acce + 2;
   uint64_t* done = tbl + 1;
+  uint64_t* rdy = done + 1;  // this CTA's router logits are computed (its weight stream may start)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Ls.tmem);
   int* misc = reinterpret_cast<int*>(sm + Ls.misc);
   int* e_id = reinterpret_cast<int*>(sm + Ls.e_id);
@@ -239,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(tbl, 1);
     mbar_init(done, 1);
+    mbar_init(rdy, 1);
     fence_mbar_init();
     misc[1] = 0;
     misc[2] = 0;
@@ -248,6 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::prefetch_tmap(&tm_d);
     tc::prefetch_tmap(&tm_ab);
   }
+  // the routing path's reads start first: the norm weights (into L2) and the router warps' expert rows (into
+  // registers; warp 6 + w computes expert 2 * CTA + w)
+  if (warp == 6 && lane == 0 && p.norm_w != nullptr) bulk_prefetch_l2(p.norm_w, static_cast<uint32_t>(H) * 2u);
+  const int r_e = blockIdx.x * 2 + (warp - 6);
+  const bool r_has = warp >= 6 && p.router && r_e < p.E;
+  const int r_esz = p.rw_dtype == MV_F32 ? 4 : (p.rw_dtype == MV_BF16 ? 2 : 1);
+  uint4 r_row[kRouterChunks];
+  if (r_has) router_row_load(static_cast<const uint8_t*>(p.rw) + static_cast<size_t>(r_e) * H * r_esz, H * r_esz, r_row);
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tmem_relinquish();
@@ -279,6 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
       const uint4* gw = reinterpret_cast<const uint4*>(p.norm_w);
       for (int m = warp; m < M; m += kThreads / 32) {
+        uint4 gpre[kMaxH / 256];  // this lane's norm-weight chunks, in flight during the sum
+#pragma unroll
+        for (int i = 0; i < kMaxH / 256; ++i)
+          if (lane + 32 * i < nch) gpre[i] = gw[lane + 32 * i];
         double ss = 0.0;
         for (int c = lane; c < nch; c += 32) {
           const uint4 v = *reinterpret_cast<const uint4*>(xb + xb_off(m, c));
@@ -292,10 +314,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         ss = warp_sum_d(ss);
         const float var = static_cast<float>(ss / static_cast<double>(H));
         const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
-        for (int c = lane; c < nch; c += 32) {
+#pragma unroll
+        for (int i = 0; i < kMaxH / 256; ++i) {
+          const int c = lane + 32 * i;
+          if (c >= nch) break;
           uint4* dst = reinterpret_cast<uint4*>(xb + xb_off(m, c));
           const uint4 v = *dst;
-          const uint4 g = gw[c];
+          const uint4 g = gpre[i];
           const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
           const uint32_t gg[4] = {g.x, g.y, g.z, g.w};
           uint32_t o[4];
@@ -364,6 +389,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       };
+      // a CTA computing router logits starts its weight stream after them: the tensor core's shared-memory reads
+      // slow the router warps' fp64 dot products several-fold, and the routing decision is the critical path
+      if (ok) ok = mbar_wait_lazy(rdy, 0u, p.ws, 0x608u, 256);
       gu_range(T_s, 0, true);
       if (ok) ok = mbar_wait_lazy(tbl, 0u, p.ws, 0x610u, 1024);
       const int U = misc[0];
@@ -498,29 +526,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ================================================================ router / table (warps 6..7)
     const int rt = tid - 192;
     auto rbar = [] { named_bar(2, kRt); };
-    // the arrival counters start from zero in every call (the workspace may hold anything: another call's
-    // layout, or the CUDA-core kernel's data): each CTA clears a share, then a grid barrier publishes it
-    {
-      const int ncnt = (p.u_max * S + HS) * 4;
-      for (int i = blockIdx.x * kRt + rt; i < ncnt; i += G * kRt) p.tc_cnt[i] = 0;
-      __threadfence();
-      rbar();
-      if (rt == 0) grid_arrive(&p.ws->pad[0]);
-    }
+    if (!p.router && rt == 0) mbar_arrive(rdy);  // no logits to compute: the weight stream starts at once
     if (p.router) {
-      const int e = blockIdx.x * 2 + (warp - 6);
-      if (e < p.E) {
+      const int e = r_e;
+      if (r_has) {
         double acc[kMaxM];
 #pragma unroll
         for (int m = 0; m < kMaxM; ++m) acc[m] = 0.0;
-        const int resz = p.rw_dtype == MV_F32 ? 4 : (p.rw_dtype == MV_BF16 ? 2 : 1);
-        const void* wrow = static_cast<const uint8_t*>(p.rw) + static_cast<size_t>(e) * H * resz;
         if (p.rw_dtype == MV_F32)
-          router_logits_sw<MV_F32>(wrow, 1.0f, xb, H, M, acc);
+          router_logits_sw<MV_F32>(r_row, 1.0f, xb, H, M, acc);
         else if (p.rw_dtype == MV_BF16)
-          router_logits_sw<MV_BF16>(wrow, 1.0f, xb, H, M, acc);
+          router_logits_sw<MV_BF16>(r_row, 1.0f, xb, H, M, acc);
         else
-          router_logits_sw<MV_I8>(wrow, decode::ldscale(p.rw_scale, e, p.rw_scale_bf16), xb, H, M, acc);
+          router_logits_sw<MV_I8>(r_row, decode::ldscale(p.rw_scale, e, p.rw_scale_bf16), xb, H, M, acc);
 #pragma unroll
         for (int m = 0; m < kMaxM; ++m) {
           if (m < M) {
@@ -530,6 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       rbar();
+      if (rt == 0) mbar_arrive(rdy);
       if (rt == 0) grid_arrive(&p.ws->bar1);
       if (rt == 0) grid_wait(&p.ws->bar1, G, p.ws, 0x680u);
       rbar();
@@ -622,6 +641,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) tc::fence_after_sync();
       return ok;
     };
+    // the arrival counters start from zero in every call (the workspace may hold anything: another call's
+    // layout, or the CUDA-core kernel's data): each CTA clears a share, then a grid barrier publishes it. The
+    // epilogue warps do it while their first accumulator fills, off the routing path.
+    {
+      const int ncnt = (p.u_max * S + HS) * 4;
+      for (int i = blockIdx.x * kEpi + et; i < ncnt; i += G * kEpi) p.tc_cnt[i] = 0;
+      __threadfence();
+      named_bar(3, kEpi);
+      if (et == 0) grid_arrive(&p.ws->pad[0]);
+    }
     const uint32_t tlane = static_cast<uint32_t>(g4 * 32) << 16;
     // SiLU(g) * u * weight as hi / lo bf16 rows of the activation buffer (static slots carry weight 1)
     auto finalize = [&](int j, int sl, const float* g, const float* u) {
