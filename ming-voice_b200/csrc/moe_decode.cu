@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
   using WT = W<INT8>;
   constexpr int kCons = CW * 32;     // consumer threads
   constexpr int kThr = kCons + 32;   // + producer warp
+  constexpr int kDG = 4;             // warps per group in the packed down phase
   constexpr bool XF = MT <= 4;       // token activations kept as split fp32 in shared memory
   constexpr int VEC = WT::vec;
   constexpr int NQ = VEC / 4;
@@ -109,6 +110,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
   float* sel_gs = sel_sc + M * p.E_alloc;                          // [M][32]
   double* red = reinterpret_cast<double*>((reinterpret_cast<uintptr_t>(sel_gs + M * 32) + 7) & ~uintptr_t(7));
   double* sel_k = red + CW * kMaxM;                                // [M][top_k]
+  float* ypart = reinterpret_cast<float*>(sel_k + M * 32);         // [u_max][nh_cap][MT] (packed down phase)
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -596,7 +598,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
   named_bar(1, kCons);
   // one warp, one w_d row: y[tok][r] += w_d[e][hd0 + r] . a[u, tok] for the tokens of expert u; row r is
   // always computed by warp r % CW, so every y element has a single writer and a fixed summation order
-  auto d_row = [&](const uint8_t* row, const float* a_u, int u, int r, float sc) {
+  auto d_row = [&](const uint8_t* row, const float* a_u, int u, int r, float sc, float* part) {
     const int ntok = e_ntok[u];
     float acc[MT][2];
 #pragma unroll
@@ -635,28 +637,39 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
     for (int t = 0; t < MT; ++t) {
       if (t < ntok) {
         const float v = warp_sum(acc[t][0] + acc[t][1]);
-        if (lane == 0) y_s[e_tok[u * MT + t] * kNhMax + r] += v;  // row r has one owner warp
+        if (lane == 0) {
+          if (part != nullptr)
+            part[t] = v;  // (expert u, row r) has one writer
+          else
+            y_s[e_tok[u * MT + t] * kNhMax + r] += v;  // row r has one owner warp
+        }
       }
     }
   };
   if (p.a_all) {
-    // packed stages: warp w computes entries w, w + CW, ... of the stage's slice of the (expert, row) sequence
+    // packed stages, each consumed by one group of kDG warps (the group owning its ring slot; the other warps
+    // skip it, and the group's arrivals count for all CW): warp i of the group computes entries i, i + kDG, ...
+    // of the stage's slice of the (expert, row) sequence into its own (expert, row) slot of ypart
     const int DP = p.DP;
     const int nent = U * nh;
+    const int ngroups = CW / kDG;
+    const int dg = warp / kDG, di = warp % kDG;
     for (int e0 = 0; e0 < nent; e0 += DP) {
       const int e1 = min(nent, e0 + DP);
       const int s = stage;
-      ok = wait_full(s) && ok;
-      advance();
-      if (ok) {
-        for (int k = 0; k < e1 - e0; ++k) {
-          const int u = (e0 + k) / nh, r = (e0 + k) % nh;
-          if (r % CW != warp) continue;  // output row r has one owner warp: deterministic sums
-          const uint8_t* row = ring + static_cast<size_t>(s) * kStageBytes + static_cast<size_t>(k) * I * WT::esz;
-          d_row(row, abuf + e_pbase[u] * I, u, r, INT8 ? dsc[u * nhc + r] : 1.0f);
+      if (s % ngroups == dg) {
+        ok = wait_full(s) && ok;
+        if (ok) {
+          for (int k = di; k < e1 - e0; k += kDG) {
+            const int u = (e0 + k) / nh, r = (e0 + k) % nh;
+            const uint8_t* row = ring + static_cast<size_t>(s) * kStageBytes + static_cast<size_t>(k) * I * WT::esz;
+            d_row(row, abuf + e_pbase[u] * I, u, r, INT8 ? dsc[u * nhc + r] : 1.0f, ypart + (u * nhc + r) * MT);
+          }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cnt(&empty_bar[s], static_cast<uint32_t>(CW / kDG));
       }
-      release(s);
+      advance();
     }
   } else {
     int cur_off = 0;  // float offset of the current expert's a rows in the region
@@ -688,7 +701,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
           for (int k = 0; k < nr; ++k) {
             if ((r0 + k) % CW != warp) continue;
             const uint8_t* row = ring + static_cast<size_t>(s) * kStageBytes + static_cast<size_t>(k) * I * WT::esz;
-            d_row(row, abuf + cur_off, u, r0 + k, INT8 ? dsc[u * nhc + r0 + k] : 1.0f);
+            d_row(row, abuf + cur_off, u, r0 + k, INT8 ? dsc[u * nhc + r0 + k] : 1.0f, nullptr);
           }
         }
         release(s);
@@ -701,6 +714,12 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
   for (int j = tid; j < M * nh; j += kCons) {
     const int t = j / nh, r = j % nh;
     float v = y_s[t * kNhMax + r];
+    if (p.a_all) {  // packed: the (expert, row) results of token t, added in expert order
+      v = 0.f;
+      for (int u = 0; u < U; ++u)
+        for (int i = 0; i < e_ntok[u]; ++i)
+          if (e_tok[u * MT + i] == t) v += ypart[(u * nhc + r) * MT + i];
+    }
     if (p.residual != nullptr) v += __uint_as_float(static_cast<uint32_t>(p.residual[t * H + hd0 + r]) << 16);
     p.out[t * H + hd0 + r] = f2bf(v);
   }
@@ -814,18 +833,19 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
                        kMaxM * kMaxNK * 8 + static_cast<size_t>(M) * p.E_alloc * 8 + static_cast<size_t>(M) * 32 * 4 +
                        8 + static_cast<size_t>(CW) * kMaxM * 8 + static_cast<size_t>(M) * 32 * 8 + 64;
   size_t region = xn_bytes > a_bytes ? xn_bytes : a_bytes;
+  const size_t ypart_bytes = static_cast<size_t>(p.u_max) * p.nh_cap * MT * 4;  // packed down-phase results
   p.a_all = 0;
   {
     size_t r_all = xn_bytes > all_bytes ? xn_bytes : all_bytes;
     r_all = (r_all + 31) & ~size_t(31);
-    if (4 * (kStageBytes + 16) + r_all + small <= 227 * 1024) {
+    if (4 * (kStageBytes + 16) + r_all + small + ypart_bytes <= 227 * 1024) {
       region = r_all;
       p.a_all = 1;
     }
   }
   region = (region + 31) & ~size_t(31);
   p.region_bytes = static_cast<int>(region);
-  const size_t fixed = ((region + small) + 15) & ~size_t(15);
+  const size_t fixed = ((region + small + (p.a_all ? ypart_bytes : 0)) + 15) & ~size_t(15);
   const size_t cap = 227 * 1024;
   // ring depth: 4 x 32 KB stages keep enough bytes in flight per SM (more stages measured slower); an
   // environment override (MINGMOE_DECODE_STAGES=2..8) exists for tuning
