@@ -101,7 +101,10 @@ struct WsHeader {
   unsigned int err_info;  // where it was raised (kernel-specific)
   unsigned int bar1;      // grid-barrier arrival counters of cooperative kernels (reset by the last CTA)
   unsigned int bar2;
-  unsigned int pad[59];
+  unsigned int pad[3];
+  unsigned long long gen1;  // generation grid barriers: count up by G per call, never reset (grid_arrive_gen)
+  unsigned long long gen2;
+  unsigned int pad2[52];
 };
 static_assert(sizeof(WsHeader) == 256, "workspace header must be 256 bytes");
 
@@ -253,6 +256,37 @@ __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
 __device__ __forceinline__ void grid_arrive(unsigned int* ctr) {
   __threadfence();
   atomicAdd(ctr, 1u);
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Generation grid barrier (one thread per CTA): the counter grows by G in every call and is never reset, so a
+// kernel needs no last-CTA epilogue. Arrive returns this call's target: the next multiple of G at or above the
+// counter (the counter is a multiple of G between calls).
+__device__ __forceinline__ unsigned long long grid_arrive_gen(unsigned long long* ctr, unsigned int G) {
+  __threadfence();
+  const unsigned long long old = atomicAdd(ctr, 1ull);
+  return old - old % G + G;
+}
+
+static __device__ __noinline__ bool grid_wait_gen(unsigned long long* ctr, unsigned long long target, WsHeader* h,
+                                                  unsigned int info) {
+  if (ld_acquire_u64(ctr) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  unsigned int ns = 32;
+  while (ld_acquire_u64(ctr) < target) {
+    __nanosleep(ns);
+    if (ns < 256) ns *= 2;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_error(h, kErrTimeout, info);
+      return false;
+    }
+  }
+  return true;
 }
 
 // One thread per CTA: wait until `target` CTAs arrived. Bounded: gives up after kWaitLimitNs, records

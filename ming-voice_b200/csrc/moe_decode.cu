@@ -21,8 +21,9 @@
 // prefetched while the consumers finish the gate/up phase, so HBM sees one continuous stream.
 //
 // Fused router (mode 1): the shared-expert slots (static ids, weight 1) need no routing, so every CTA
-// starts streaming their gate/up rows at once. Meanwhile the first ceil(E/8) CTAs compute the router logits
-// (one warp per expert, fp64 accumulation), a first grid barrier publishes them, and every CTA then makes the
+// starts streaming their gate/up rows at once. Meanwhile warp w of CTA b computes the logit of expert w * G + b
+// (fp64 accumulation; spread over CTAs so no CTA starts its gate/up share late, and the router rows are
+// prefetched into L2 at kernel entry), a first grid barrier publishes them, and every CTA then makes the
 // (deterministic, identical) top-k selection itself and continues with the routed experts.
 //
 // Numerics: fp32 accumulation and intermediates; int8 weights are dequantised per element as
@@ -287,8 +288,20 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
     if (lane == 0) mbar_arrive(&empty_bar[s]);
   };
 
+  // this thread's first output element's residual, read now rather than after the down phase
+  const float res_pre = (p.residual != nullptr && tid < M * nh)
+                            ? __uint_as_float(static_cast<uint32_t>(p.residual[(tid / nh) * H + hd0 + tid % nh]) << 16)
+                            : 0.f;
+
   // ---- prologue: token rows (RMSNorm or copy) -> xn (bf16) and, for M <= 4, xf (split fp32)
   {
+    // the router row of this warp's logit starts towards L2 before the weight stream fills the memory queues
+    if (p.router && lane == 0 && warp * G + static_cast<int>(blockIdx.x) < p.E) {
+      const int resz = p.rw_dtype == MV_F32 ? 4 : (p.rw_dtype == MV_BF16 ? 2 : 1);
+      bulk_prefetch_l2(static_cast<const uint8_t*>(p.rw) +
+                           static_cast<size_t>(warp * G + static_cast<int>(blockIdx.x)) * H * resz,
+                       static_cast<uint32_t>(H * resz));
+    }
     const int nv = H / 8;  // 16-byte vectors per row
     // the norm weight's first vector per thread is fetched with x, so both latencies overlap
     const uint4 g_pref = (p.norm_w != nullptr && tid < nv) ? reinterpret_cast<const uint4*>(p.norm_w)[tid]
@@ -356,12 +369,13 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
     named_bar(1, kCons);
   }
 
-  // ---- gate/up consumer for one walk. The consumer warps form NG = CW / RG groups; group g computes every
-  // NG-th stage (the g-th of each NG), warp gi of the group the complete gate row gi and up row gi, i.e. the
-  // activation a[gi] of the expert's tokens (no partial sums). All warps still wait on and release every stage.
+  // ---- gate/up consumer for one walk. The consumer warps form NG = CW / RG groups; group g owns the ring slots
+  // s with s % NG == g and alone waits on and releases their stages (each of its RG arrivals counts CW / RG, so
+  // the empty barrier still completes after CW), warp gi of the group computing the complete gate row gi and up
+  // row gi, i.e. the activation a[gi] of the expert's tokens (no partial sums). A slot always belongs to one
+  // group, so a warp never waits on a phase more than one ahead of the barrier.
   const int gi = warp % RG, gq = warp / RG;
   const int NG = CW / RG;
-  int gu_count = 0;
   auto gu_consume = [&](GuWalk walk, bool is_static, int sc_base) {
     int u, i0, ni;
     long long r0w;
@@ -378,10 +392,10 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
       }
       for (int s0 = 0; s0 < ni; s0 += RG) {
         const int nr = min(RG, ni - s0);
-        const bool mine = (gu_count % NG) == gq && gi < nr;
-        ++gu_count;
         const int s = stage;
-        ok = wait_full(s) && ok;
+        const bool grp = (s % NG) == gq;  // the group owning this ring slot consumes the stage
+        const bool mine = grp && gi < nr;
+        if (grp) ok = wait_full(s) && ok;
         advance();
         if (ok && mine) {
           const uint8_t* st = ring + static_cast<size_t>(s) * kStageBytes;
@@ -480,14 +494,18 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
             }
           }
         }
-        release(s);
+        if (grp) {  // the group's RG arrivals count for all CW consumer warps
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cnt(&empty_bar[s], static_cast<uint32_t>(CW / RG));
+        }
       }
     }
   };
 
-  // ---- router logits (mode 1, first ceil(E/CW) CTAs), the static (shared-expert) rows, then the routing
+  // ---- router logits (mode 1, expert w * G + b on warp w of CTA b), the static (shared-expert) rows, then the
+  // routing
   if (p.router) {
-    const int e = blockIdx.x * CW + warp;
+    const int e = warp * G + static_cast<int>(blockIdx.x);
     if (e < p.E) {
       double acc[MT];
 #pragma unroll
@@ -505,10 +523,11 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
       }
     }
     named_bar(1, kCons);
-    if (tid == 0) grid_arrive(&p.ws->bar1);  // (fence + arrive by one thread after the CTA barrier)
+    unsigned long long tgt1 = 0;
+    if (tid == 0) tgt1 = grid_arrive_gen(&p.ws->gen1, G);  // (fence + arrive by one thread after the CTA barrier)
     gu_consume(GuWalk{s_lo, s_hi, I, 0}, true, 0);
     named_bar(1, kCons);
-    if (tid == 0) grid_wait(&p.ws->bar1, G, p.ws, 0x300u);
+    if (tid == 0) grid_wait_gen(&p.ws->gen1, tgt1, p.ws, 0x300u);
     named_bar(1, kCons);
     // every CTA makes the same selection from the published logits, all consumer threads in parallel
     const route::SelectCfg cfg{p.route_mode, p.E, p.top_k, p.n_group, p.topk_group, p.rscale, p.rbias};
@@ -569,8 +588,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
   // ---- grid barrier: every CTA's activations are in a_g
   named_bar(1, kCons);
   if (tid == 0) {
-    grid_arrive(&p.ws->bar2);
-    grid_wait(&p.ws->bar2, G, p.ws, 0x400u);
+    const unsigned long long tgt2 = grid_arrive_gen(&p.ws->gen2, G);
+    grid_wait_gen(&p.ws->gen2, tgt2, p.ws, 0x400u);
   }
   named_bar(1, kCons);
 
@@ -720,20 +739,11 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
         for (int i = 0; i < e_ntok[u]; ++i)
           if (e_tok[u * MT + i] == t) v += ypart[(u * nhc + r) * MT + i];
     }
-    if (p.residual != nullptr) v += __uint_as_float(static_cast<uint32_t>(p.residual[t * H + hd0 + r]) << 16);
+    if (p.residual != nullptr)
+      v += j == tid ? res_pre : __uint_as_float(static_cast<uint32_t>(p.residual[t * H + hd0 + r]) << 16);
     p.out[t * H + hd0 + r] = f2bf(v);
   }
-
-  // ---- the last CTA resets the grid-barrier counters for the next call
-  named_bar(1, kCons);
-  if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(&p.ws->counter, 1u) == static_cast<unsigned int>(G - 1)) {
-      atomicExch(&p.ws->bar1, 0u);
-      atomicExch(&p.ws->bar2, 0u);
-      atomicExch(&p.ws->counter, 0u);
-    }
-  }
+  // (generation grid barriers: nothing to reset for the next call)
 }
 
 }  // namespace decode
