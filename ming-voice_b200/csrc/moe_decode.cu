@@ -665,6 +665,63 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
       }
     }
   };
+  // One token (MT == 1): the expert's activation chunks this lane needs stay in registers across the rows of
+  // that expert (kAC floats: the lane's chunks ch = lane + 32 i), so a row costs only its weight reads from
+  // shared memory. Same operations in the same order as d_row, so the results are identical.
+  constexpr int kAC = 48;
+  constexpr int kACIt = kAC / VEC;
+  const bool a_regs = MT == 1 && I / VEC <= 32 * kACIt;
+  float ac[kACIt][VEC];
+  int ac_u = -1;
+  auto d_row_m1 = [&](const uint8_t* row, int u, float sc, float* part) {
+    const int nvec = I / VEC;
+    if (u != ac_u) {
+      const float* a_u = abuf + e_pbase[u] * I;
+#pragma unroll
+      for (int i = 0; i < kACIt; ++i) {
+        const int ch = lane + 32 * i;
+        if (ch < nvec) {
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) {
+            const float4 av = *reinterpret_cast<const float4*>(a_u + ch * 4 + q * (I / NQ));
+            ac[i][4 * q] = av.x;
+            ac[i][4 * q + 1] = av.y;
+            ac[i][4 * q + 2] = av.z;
+            ac[i][4 * q + 3] = av.w;
+          }
+        }
+      }
+      ac_u = u;
+    }
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kACIt; ++i) {
+      const int ch = lane + 32 * i;
+      if (ch < nvec) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(row + ch * 16);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        if (INT8) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float w0, w1, w2, w3;
+            i8x4_to_f32(ww[q], w0, w1, w2, w3);
+            fmul2(w0, w1, w0, w1, sc);
+            fmul2(w2, w3, w2, w3, sc);
+            ffma2(acc0, acc1, w0, w1, ac[i][4 * q], ac[i][4 * q + 1]);
+            ffma2(acc0, acc1, w2, w3, ac[i][4 * q + 2], ac[i][4 * q + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            ffma2(acc0, acc1, bf16lo(ww[2 * q]), bf16hi(ww[2 * q]), ac[i][4 * q], ac[i][4 * q + 1]);
+            ffma2(acc0, acc1, bf16lo(ww[2 * q + 1]), bf16hi(ww[2 * q + 1]), ac[i][4 * q + 2], ac[i][4 * q + 3]);
+          }
+        }
+      }
+    }
+    const float v = warp_sum(acc0 + acc1);
+    if (lane == 0) part[0] = v;
+  };
   if (p.a_all) {
     // packed stages, each consumed by one group of kDG warps (the group owning its ring slot; the other warps
     // skip it, and the group's arrivals count for all CW): warp i of the group computes entries i, i + kDG, ...
@@ -682,7 +739,10 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
           for (int k = di; k < e1 - e0; k += kDG) {
             const int u = (e0 + k) / nh, r = (e0 + k) % nh;
             const uint8_t* row = ring + static_cast<size_t>(s) * kStageBytes + static_cast<size_t>(k) * I * WT::esz;
-            d_row(row, abuf + e_pbase[u] * I, u, r, INT8 ? dsc[u * nhc + r] : 1.0f, ypart + (u * nhc + r) * MT);
+            if (a_regs)
+              d_row_m1(row, u, INT8 ? dsc[u * nhc + r] : 1.0f, ypart + (u * nhc + r) * MT);
+            else
+              d_row(row, abuf + e_pbase[u] * I, u, r, INT8 ? dsc[u * nhc + r] : 1.0f, ypart + (u * nhc + r) * MT);
           }
         }
         __syncwarp();
