@@ -92,6 +92,11 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Arrive on a named barrier without waiting (producer / consumer hand-off: the waiting side uses named_bar).
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------ error flag
 
 // Workspace header layout (first 256 bytes of every kernel workspace).

@@ -525,8 +525,6 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
     named_bar(1, kCons);
     unsigned long long tgt1 = 0;
     if (tid == 0) tgt1 = grid_arrive_gen(&p.ws->gen1, G);  // (fence + arrive by one thread after the CTA barrier)
-    gu_consume(GuWalk{s_lo, s_hi, I, 0}, true, 0);
-    named_bar(1, kCons);
     if (tid == 0) grid_wait_gen(&p.ws->gen1, tgt1, p.ws, 0x300u);
     named_bar(1, kCons);
     // every CTA makes the same selection from the published logits, all consumer threads in parallel
@@ -561,7 +559,15 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
                        misc, bitmap, p.ws, tid, kCons, [] { named_bar(1, kCons); });
     }
   }
-  named_bar(2, kThr);  // the expert table is published (by the producer warp, or by the consumers above)
+  if (p.router) {
+    // the table goes to every consumer and, without waiting, to the producer (which streams the static rows
+    // first and then waits for it); the routing decision came first, the static rows the ring holds follow
+    named_bar(1, kCons);
+    named_bar_arrive(2, kThr);
+    gu_consume(GuWalk{s_lo, s_hi, I, 0}, true, 0);
+  } else {
+    named_bar(2, kThr);  // the expert table is published by the producer warp
+  }
 
   const int U = misc[0];
   const long long R = static_cast<long long>(U - n_static) * I;
