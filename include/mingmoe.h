@@ -170,6 +170,8 @@ MV_API size_t mv_moe_align_workspace_bytes(int P, int E1);
  * bf16 (exact) in the workspace and the scales multiply the fp32 products, as the reference's int8 kernels do.
  * workspace: mv_moe_prefill_workspace_bytes(N, NK, H, I, E1, w_dtype) bytes, 256-byte aligned, header zeroed
  * (int8 adds bf16 copies of the stacks: E1 * 3 * I * H * 2 bytes).
+ * An id of -1 marks "no pair" (an expert held by another rank in expert-parallel prefill): the pair is skipped;
+ * any other id outside [0, E1) is an error (recorded in the workspace, the pair skipped).
  * Requirements: H a multiple of 256, I a multiple of 128, E1 <= 512, 16-byte aligned pointers/strides. */
 MV_API int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids, int ids_dtype,
                           const float* wts, int N, int NK, const void* residual, long long residual_stride, void* out,

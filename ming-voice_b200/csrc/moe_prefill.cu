@@ -6,7 +6,8 @@
 // Pipeline (seven launches, no host synchronisation, capture-safe):
 //   1. align_*_kernel  stable counting sort of the (token, slot) pairs by expert, each expert's run padded to
 //                      128 rows (three launches); the same sorted_ids / bexp arrays the reference builds
-//                      (pad id = P, unused block = -1).
+//                      (pad id = P, unused block = -1). Pairs with id -1 are left out (expert-parallel prefill
+//                      marks the pairs another rank computes that way).
 //   2. gather_kernel   xs[r] = x[token of sorted pair r] (bf16, zero rows for pads) and y32 = residual (fp32).
 //   3. gemm_kernel<0>  per 128-pair block and 128-column slice of the intermediate dimension:
 //                      [gate | up] = xs_blk . W_gu[e]^T as ONE 128 x 256 tcgen05 tile (gate rows n0.., up rows
@@ -73,7 +74,7 @@ __global__ void __launch_bounds__(kChunk) align_count_kernel(const void* __restr
     const int e = load_id(ids, ids_i64, p);
     if (e >= 0 && e < E1)
       atomicAdd(&sh[e], 1);
-    else
+    else if (e != -1)  // -1: no pair (an expert held by another rank); anything else is an error
       raise_error(ws, kErrBadExpert, static_cast<unsigned int>(p));
   }
   __syncthreads();

@@ -8,14 +8,14 @@ replicating them costs 17 MB per expert of the 180 GB on each GPU.
 
 A prefill step on a rank's own packed tokens:
   1. RMSNorm and routing locally (mv_rmsnorm, mv_route);
-  2. the (token, routed expert) pairs sorted by owner rank (stable, so every rank sends in token order);
-     pair counts exchanged with one all-to-all, then the token rows (bf16 [H]) and their metadata (slot of the
-     expert on its owner, routing weight) with all-to-all-v -- the one exchange step of the block (a
-     replicated expert's pairs go to the rank itself, i.e. stay local);
-  3. the owner computes weight * expert(row) for every received pair with the tcgen05 grouped GEMM
-     (mv_moe_prefill, one expert per row);
-  4. the weighted outputs travel back (all-to-all-v, the reverse split) and are added at the origin in fp32,
-     together with the shared expert (computed locally) and the residual.
+  2. every pair whose expert this rank holds (the replicated hot experts, its share of the cold ones, the
+     shared expert) is computed at once, with the residual, by one tcgen05 grouped-GEMM pass over the rank's
+     own tokens (mv_moe_prefill; the other pairs carry id -1, which the expert sort skips);
+  3. the other pairs, sorted by owner rank (stable, so every rank sends in token order): pair counts exchanged
+     with one all-to-all, then the token rows (bf16 [H]) and their metadata (slot of the expert on its owner,
+     routing weight) with all-to-all-v -- the one exchange step of the block;
+  4. the owner computes weight * expert(row) for every received pair (mv_moe_prefill, one expert per row), the
+     weighted outputs travel back (all-to-all-v, the reverse split) and are added at the origin in fp32.
 
 The exchange sizes are data dependent, so a step synchronises the host once (the split sizes); prefill is not
 graph-captured. No kernel reads another GPU's memory: everything remote arrives through NCCL.
@@ -72,16 +72,11 @@ class EPMoeBlock:
         b = self.block
         return moe.experts(x, b.w_gu, b.w_d, ids, wts, s_gu=b.s_gu, s_d=b.s_d, residual=residual)
 
-    def dispatch_plan(self, ids):
-        """Sort the routed pairs by owner rank. Returns (order [P] pair indices sorted by owner, counts [world])."""
-        K = self.block.top_k
-        routed = ids[:, :K].reshape(-1).long()
-        if self.owner.device != routed.device:
-            self.owner, self.slot = self.owner.to(routed.device), self.slot.to(routed.device)
-        owner = self.owner[routed]
-        order = torch.sort(owner, stable=True).indices
-        counts = torch.bincount(owner, minlength=self.world)
-        return order, counts
+    def _local(self, xn, ids, wts, x):
+        """x + sum over this rank's pairs (ids -1 = a pair owned elsewhere, skipped) in one grouped-GEMM pass."""
+        if self.experts_fn == self._experts_cuda:
+            return self._experts_cuda(xn, ids, wts, residual=x)
+        return (x.float() + self.experts_fn(xn, ids, wts).float()).to(x.dtype)
 
     def _a2a(self, out, inp, out_splits, in_splits):
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
@@ -98,42 +93,53 @@ class EPMoeBlock:
         else:
             xn = x
         ids, wts, _ = b.route(xn)
+        if self.owner.device != dev:
+            self.owner, self.slot = self.owner.to(dev), self.slot.to(dev)
+        routed = ids[:, :K].long()
+        own = self.owner[routed]  # [N, K] the rank holding each routed pair's expert
+        slot = self.slot[routed]  # its stack index there
+        ids_loc = torch.where(own == self.rank, slot, torch.full_like(slot, -1))
+        if self.n_shared:
+            ids_loc = torch.cat([ids_loc, ids[:, K:].to(ids_loc.dtype)], 1)
+        # the pairs of this rank (replicated experts, its share of the cold ones, the shared expert) and the
+        # residual: one grouped-GEMM pass over its own tokens, enqueued before the exchange's host synchronisation
+        y = self._local(xn, ids_loc.to(torch.int32).contiguous(), wts, x)
+        if self.world == 1:
+            return y
 
-        order, counts = self.dispatch_plan(ids)
+        # the other pairs: sorted by owner (stable, so in token order per owner), exchanged, computed, returned
+        flat_own = own.reshape(-1)
+        key = torch.where(flat_own == self.rank, torch.full_like(flat_own, self.world), flat_own)
+        order_all = torch.sort(key, stable=True).indices
+        counts = torch.bincount(key, minlength=self.world + 1)[: self.world].contiguous()
         recv_counts = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
         in_splits = counts.tolist()
         out_splits = recv_counts.tolist()  # (the one host synchronisation of the step)
-        R = sum(out_splits)
+        n_send, R = sum(in_splits), sum(out_splits)
 
+        order = order_all[:n_send]
         tok = torch.div(order, K, rounding_mode="floor")
         send_rows = xn.index_select(0, tok)
-        routed = ids[:, :K].reshape(-1).long()
-        send_meta = torch.stack([self.slot[routed[order]].to(torch.float32), wts[:, :K].reshape(-1)[order]], 1)
+        send_meta = torch.stack([slot.reshape(-1)[order].to(torch.float32),
+                                 wts[:, :K].reshape(-1)[order].to(torch.float32)], 1)
         recv_rows = torch.empty(R, H, dtype=xn.dtype, device=dev)
         recv_meta = torch.empty(R, 2, dtype=torch.float32, device=dev)
         self._a2a(recv_rows, send_rows, out_splits, in_splits)
         self._a2a(recv_meta, send_meta, out_splits, in_splits)
-
         if R > 0:
             lid = recv_meta[:, 0].round().to(torch.int32).unsqueeze(1)
             lw = recv_meta[:, 1].contiguous().unsqueeze(1)
             y_pairs = self.experts_fn(recv_rows, lid, lw)
         else:
             y_pairs = torch.empty(0, H, dtype=xn.dtype, device=dev)
-
-        back = torch.empty(order.numel(), H, dtype=y_pairs.dtype, device=dev)
+        back = torch.empty(n_send, H, dtype=y_pairs.dtype, device=dev)
         self._a2a(back, y_pairs.contiguous(), in_splits, out_splits)
-
-        # shared expert locally (the slots after this rank's routed stacks, weight 1)
-        y = x.to(torch.float32, copy=True)  # (never an alias of the caller's tokens)
-        if self.n_shared:
-            sid = torch.arange(self.n_local, self.n_local + self.n_shared, dtype=torch.int32, device=dev)
-            s_ids = sid.unsqueeze(0).expand(N, -1).contiguous()
-            s_w = torch.ones(N, self.n_shared, dtype=torch.float32, device=dev)
-            y += self.experts_fn(xn, s_ids, s_w).float()
-        y.index_add_(0, tok, back.float())
-        return y.to(x.dtype)
+        if n_send == 0:
+            return y
+        y32 = y.to(torch.float32)
+        y32.index_add_(0, tok, back.to(torch.float32))
+        return y32.to(x.dtype)
 
 
 def shard_block_params(p: dict, rank: int, world: int, E: int, replicated=()):

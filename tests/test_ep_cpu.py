@@ -41,8 +41,11 @@ def _worker(rank, world, port, seed, replicated, q):
         bias = O.zipf_bias(E)
         loc = shard_block_params(p, rank, world, E, replicated)
 
-        def experts_fn(x, ids, wts):  # weight * expert(x) per row, this rank's stacks
-            return O.moe_experts(x, loc["w_gu"], loc["w_d"], ids.long(), wts)
+        def experts_fn(x, ids, wts):  # weight * expert(x) per row, this rank's stacks; id -1 = not here
+            ids = ids.long()
+            skip = ids < 0
+            return O.moe_experts(x, loc["w_gu"], loc["w_d"], torch.where(skip, 0, ids),
+                                 torch.where(skip, torch.zeros_like(wts), wts))
 
         ep = EPMoeBlock(_RefBlock(p, loc["shared_ids"], bias), E, replicated=replicated, experts_fn=experts_fn)
         x = O.make_tokens(13 + 7 * rank, H=H, seed=seed + rank, dtype=torch.float32)

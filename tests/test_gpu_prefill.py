@@ -168,3 +168,43 @@ def test_prefill_block_int8_reference_model_fp32_scales():
     y_ref, _, _, _ = O.moe_block(x, p, top_k=8, router="sigmoid_group")
     close(blk.prefill(x.cuda()), y_ref)
     no_device_errors()
+
+
+def test_prefill_skipped_pairs(base_params, base_params_gpu):
+    """id -1 = a pair computed elsewhere (expert-parallel prefill): left out silently, the rest unchanged."""
+    p, pg = base_params, base_params_gpu
+    x = O.make_tokens(200, seed=9)
+    g = torch.Generator().manual_seed(9)
+    ids = torch.randint(0, 66, (200, 8), generator=g)
+    wts = torch.rand(200, 8, generator=g)
+    skip = torch.rand(200, 8, generator=g) < 0.3
+    ref = O.moe_experts(x, p["w_gu"], p["w_d"], torch.where(skip, 0, ids), torch.where(skip, 0.0, wts))
+    got = prefill.experts(x.cuda(), pg["w_gu"], pg["w_d"], torch.where(skip, -1, ids).int().cuda(), wts.cuda(),
+                          residual=x.cuda())
+    close(got, ref + x.float())
+    no_device_errors()
+
+
+def test_ep_prefill_one_rank():
+    """The expert-parallel block on a world of one (NCCL): every pair local, output = the single-GPU block."""
+    import os
+    import socket
+    import torch.distributed as dist
+    from mingmoe.block import MoeBlock
+    from mingmoe.ep import EPMoeBlock, shard_block_params
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    try:
+        p = O.make_block_params(seed=7, H=1024, I=512, E=16, I_s=1024)
+        bias = O.zipf_bias(16)
+        loc = shard_block_params(p, 0, 1, 16, replicated=(0, 1))
+        ep = EPMoeBlock(MoeBlock.from_params(loc, router_bias=bias), 16, replicated=(0, 1))
+        x = O.make_tokens(300, H=1024, seed=3)
+        ref, _, _, _ = O.moe_block(x, p, top_k=6, bias=bias)
+        close(ep.forward(x.cuda()), ref)
+        no_device_errors()
+    finally:
+        dist.destroy_process_group()
