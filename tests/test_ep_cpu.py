@@ -1,4 +1,4 @@
-"""Expert-parallel prefill host logic (dispatch plan, all-to-all exchange, combine) on CPU with 2 gloo ranks.
+"""Expert-parallel prefill host logic (local pass, all-to-all exchange, combine) on CPU with 2 and 4 gloo ranks.
 
 The experts themselves are the oracle's (this checks the exchange and bookkeeping, not the kernels); each
 rank's EP output must equal the single-process block on its own tokens."""
@@ -65,12 +65,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("seed,replicated", [(0, ()), (5, ()), (3, (0, 1, 2))])
-def test_ep_prefill_two_ranks_matches_single_block(seed, replicated):
+@pytest.mark.parametrize("seed,replicated,world", [(0, (), 2), (5, (), 2), (3, (0, 1, 2), 2), (4, (0, 1), 4)])
+def test_ep_prefill_ranks_match_single_block(seed, replicated, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, seed, replicated, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, seed, replicated, q)) for r in range(world)]
     for pr in procs:
         pr.start()
     for pr in procs:
@@ -78,9 +78,9 @@ def test_ep_prefill_two_ranks_matches_single_block(seed, replicated):
     for pr in procs:
         if pr.is_alive():
             pr.kill()
-    res = dict(q.get(timeout=5) for _ in range(2))
+    res = dict(q.get(timeout=5) for _ in range(world))
     assert all(pr.exitcode == 0 for pr in procs)
-    assert res[0] < 1e-4 and res[1] < 1e-4, res
+    assert all(v < 1e-4 for v in res.values()), res
 
 
 def test_placement_tables():
