@@ -111,9 +111,11 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-def make_stack(device, layers, seed=3):
-    """16 blocks of random N(0, 0.02) weights, generated on the device (seeded)."""
+def make_stack(device, layers, seed=3, int8=False):
+    """16 blocks of random N(0, 0.02) weights, generated on the device (seeded). int8: every expert, shared and
+    router weight quantised per output row (symmetric, scale max|w|/127 stored bf16)."""
     from mingmoe.block import MoeBlock
+    import fused_moe
     g = torch.Generator(device=device).manual_seed(seed)
     blocks = []
     for _ in range(layers):
@@ -122,8 +124,62 @@ def make_stack(device, layers, seed=3):
         w_d = (torch.randn(E1, H, I, generator=g, device=device) * 0.02).to(torch.bfloat16)
         rw = (torch.randn(E, H, generator=g, device=device) * 0.02).to(torch.bfloat16)
         nw = torch.ones(H, dtype=torch.bfloat16, device=device)
-        blocks.append(MoeBlock(w_gu, w_d, rw, nw, top_k=TOPK, shared_ids=tuple(range(E, E1)), eps=1e-6))
+        if int8:
+            q_gu, s_gu = fused_moe.quantize_rows_int8(w_gu, scale_dtype=torch.bfloat16)
+            q_d, s_d = fused_moe.quantize_rows_int8(w_d, scale_dtype=torch.bfloat16)
+            q_rw, s_rw = fused_moe.quantize_rows_int8(rw, scale_dtype=torch.bfloat16)
+            del w_gu, w_d, rw
+            blocks.append(MoeBlock(q_gu, q_d, q_rw, nw, top_k=TOPK, shared_ids=tuple(range(E, E1)), eps=1e-6,
+                                   s_gu=s_gu, s_d=s_d, router_s=s_rw))
+        else:
+            blocks.append(MoeBlock(w_gu, w_d, rw, nw, top_k=TOPK, shared_ids=tuple(range(E, E1)), eps=1e-6))
     return blocks
+
+
+def int8_decode_lines(dev, steps, warmup, layers=16, Md=1):
+    """BASELINE configs[2] (int8 weights, bf16 scales) at decode M=1, through the same 16-layer graph chain as the
+    headline: us per block-token and its HBM roofline (int8 bytes + bf16 scales)."""
+    from oracle import moe_oracle as O
+    blocks = make_stack(dev, layers, seed=4, int8=True)
+    bufs = [torch.empty(Md, H, dtype=torch.bfloat16, device=dev) for _ in range(layers + 1)]
+    bufs[0].copy_(O.make_tokens(Md, seed=3).to(dev))
+    ids = torch.empty(Md, TOPK + 2, dtype=torch.int32, device=dev)
+
+    def step():
+        for layer, blk in enumerate(blocks):
+            blk.decode(bufs[layer], out=bufs[layer + 1], ids=ids if layer == 0 else None)
+
+    step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        step()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
+    s_ev.record()
+    for _ in range(steps):
+        graph.replay()
+    e_ev.record()
+    torch.cuda.synchronize()
+    us = s_ev.elapsed_time(e_ev) / steps * 1e3 / layers
+    U = O.distinct_experts(ids.cpu()[:, :TOPK])
+    byts = O.decode_bytes(U, M=Md, esz=1, scale_bytes=2)
+    peak, _ = peaks()
+    achieved = byts / (us * 1e-6) / 1e9
+    del graph, blocks
+    torch.cuda.empty_cache()
+    return {"metric": "int8 decode us/token (BASELINE configs[2], M=1, 16-layer graph chain)",
+            "value": round(us / Md, 3), "unit": "us/token", "bytes_per_block": byts,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4)}}
 
 
 def cpu_block_time_us(reps=5):
@@ -359,6 +415,9 @@ def run_ours(args):
             pre = ep_prefill_lines(dev, world, rank, max(3, min(args.steps, 20)), args.warmup)
         else:
             pre = prefill_lines(dev, max(3, min(args.steps, 50)), args.warmup)
+    q8 = None
+    if world == 1 and not args.no_int8 and Md == 1:
+        q8 = int8_decode_lines(dev, max(3, min(args.steps, 300)), args.warmup, layers=LAYERS)
     peak, peak_kind = peaks()
     byts = O.decode_bytes(U, M=Md)  # algorithmic bytes of one block step
     achieved = byts / (us_per_block * 1e-6) / 1e9
@@ -396,6 +455,8 @@ def run_ours(args):
                                            "unit": "TFLOP/s", "frac": round(pre["tflops"] / (tf_peak * world), 4),
                                            "note": f"algorithmic FLOPs / pass time; peak {tf_kind}"
                                                    + (f" x {world} GPUs" if world > 1 else "")}}
+        if q8 is not None:
+            out["int8_decode"] = q8
     if world > 1:
         torch.distributed.barrier()
         del graph
@@ -412,6 +473,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="blocks in the chain (1 = the small profiling case)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) measurement")
+    ap.add_argument("--no-int8", action="store_true", help="skip the int8 decode (configs[2]) measurement")
     ap.add_argument("--decode-m", type=int, default=1, choices=range(1, 17), metavar="M",
                     help="tokens per decode step (1 = the headline; 2..16 = the other configs[1] points)")
     ap.add_argument("--prefill-only", action="store_true",
