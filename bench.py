@@ -286,7 +286,7 @@ def prefill_lines(dev, steps, warmup):
     del graph, y
     return {"tokens": N, "us_per_pass": round(us, 1), "tokens_per_s": round(N / us * 1e6, 0),
             "tflops": round(flops / us / 1e6, 1), "e2e_tokens_per_s": round(N / us_e2e * 1e6, 0),
-            "launches_per_pass": 10, "flops_per_pass": flops}
+            "launches_per_pass": 9, "flops_per_pass": flops}
 
 
 def ep_prefill_lines(dev, world, rank, steps, warmup):

@@ -222,6 +222,10 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Orders this thread's generic-proxy global accesses with async-proxy (TMA) accesses: a writer before it
+// publishes data that TMA loads will read, a reader after it has acquired such data and before its TMA loads.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 // Bulk prefetch of global memory into L2 (no destination, nothing to wait for). `src` 16-byte aligned, `bytes` a
 // multiple of 16. Used to start small latency-critical reads (norm weights) before the weight stream fills the
 // memory queues.

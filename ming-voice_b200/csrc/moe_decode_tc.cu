@@ -135,7 +135,6 @@ __device__ __forceinline__ float ldcg(const float* p) {
   return v;
 }
 
-__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // The router warps read their expert rows at kernel entry, into registers (16-byte chunks c = lane + 32 i of
 // the row), and compute the logits once the tokens are normalised.

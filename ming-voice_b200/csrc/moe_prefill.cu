@@ -3,22 +3,25 @@
 // mv_moe_prefill replaces fused_moe.fused_moe_prefill (ming-voice fused_moe.py:176-196; kernels
 // _moe_gu_grouped :93-121, _moe_down_grouped :125-148) and mv_moe_align replaces _align_blocks (:154-173).
 //
-// Pipeline (seven launches, no host synchronisation, capture-safe):
+// Pipeline (six launches, no host synchronisation, capture-safe):
 //   1. align_*_kernel  stable counting sort of the (token, slot) pairs by expert, each expert's run padded to
 //                      128 rows (three launches); the same sorted_ids / bexp arrays the reference builds
 //                      (pad id = P, unused block = -1). Pairs with id -1 are left out (expert-parallel prefill
 //                      marks the pairs another rank computes that way).
 //   2. gather_kernel   xs[r] = x[token of sorted pair r] (bf16, zero rows for pads) and y32 = residual (fp32).
-//   3. gemm_kernel<0>  per 128-pair block and 128-column slice of the intermediate dimension:
+//   3. gemm_kernel     one persistent cooperative launch over two tile sequences:
+//                      gate/up tiles, per 128-pair block and 128-column slice of the intermediate dimension:
 //                      [gate | up] = xs_blk . W_gu[e]^T as ONE 128 x 256 tcgen05 tile (gate rows n0.., up rows
-//                      I+n0.. side by side in shared memory), epilogue a = bf16(silu(gate) * up).
-//   4. gemm_kernel<1>  per block and 256-column slice of H: o = a_blk . W_d[e]^T, epilogue
-//                      y32[token] += weight * o (fp32 vector reductions; pads skipped).
-//   5. finalize_kernel out = bf16(y32).
-// The GEMMs are persistent (one CTA per SM) and warp-specialised: warp 0 issues TMA loads into a 4-deep ring
-// of 48 KB stages (A 128x64, B 256x64 bf16, 128-byte swizzle), warp 1 issues tcgen05.mma (M=128, N=256,
-// K=16) into one of two TMEM accumulators (2 x 256 fp32 columns), warps 2-5 drain the other accumulator
-// (tcgen05.ld) while the next tile accumulates. Every wait is bounded (errors go to the workspace header).
+//                      I+n0.. side by side in shared memory), epilogue a = bf16(silu(gate) * up);
+//                      then down tiles, per block and 256-column slice of H: o = a_blk . W_d[e]^T, epilogue
+//                      y32[token] += weight * o (fp32 vector reductions; pads skipped). A down tile starts as soon
+//                      as its block's gate/up tiles are stored (per-block counters), so the last gate/up wave and
+//                      the first down wave overlap.
+//   4. finalize_kernel out = bf16(y32).
+// The GEMM kernel is warp-specialised: warp 0 issues TMA loads into a 4-deep ring of 48 KB stages (A 128x64,
+// B 256x64 bf16, 128-byte swizzle), warp 1 issues tcgen05.mma (M=128, N=256, K=16) into one of two TMEM
+// accumulators (2 x 256 fp32 columns), warps 2-5 drain the other accumulator (tcgen05.ld) while the next tile
+// accumulates. Every wait is bounded (errors go to the workspace header).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -175,8 +178,11 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint16_t* __restrict_
                                                      const int* __restrict__ sorted, const int* __restrict__ nb_used,
                                                      int NK, int P, int H, uint16_t* __restrict__ xs,
                                                      const uint16_t* __restrict__ residual, long long r_stride,
-                                                     float* __restrict__ y32, int N) {
+                                                     float* __restrict__ y32, int N, int* __restrict__ ready,
+                                                     int nb_max) {
   const int lane = threadIdx.x & 31;
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nb_max; i += blockDim.x) ready[i] = 0;
   const long long rows_xs = static_cast<long long>(*nb_used) * kBM;
   const long long total = rows_xs + N;
   const int nv = H / 8;  // 16-byte vectors per row
@@ -283,10 +289,26 @@ __device__ __forceinline__ float ld_scale(const void* base, long long i, int bf1
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
 
-// KIND 0: gate/up + SwiGLU, KIND 1: down + weighted scatter-add.
-template <int KIND>
-__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                           const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+// Both GEMMs in one persistent launch. The tile sequence is the gate/up tiles (block-major) followed by the down
+// tiles; CTA c takes tiles c, c + G, ... in order. A down tile of block b needs all gate/up tiles of b stored:
+// each gate/up epilogue warp counts its 32 rows into ready[b] (release), and the producer waits (acquire,
+// bounded) before loading the activation tile. Those gate/up tiles come earlier in the sequence and every CTA
+// processes its tiles in order, so with all CTAs resident (cooperative launch) the wait always ends; it lets
+// the down tiles start while the last gate/up wave drains instead of after it.
+__device__ __forceinline__ void tile_of(int tile, int T0, const GemmArgs& g0, const GemmArgs& g1, int& ph, int& blk,
+                                        int& nt) {
+  ph = tile >= T0;
+  const int local = ph ? tile - T0 : tile;
+  const int n = ph ? g1.n_tiles : g0.n_tiles;
+  blk = local / n;
+  nt = local - blk * n;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA0,
+                                                           const __grid_constant__ CUtensorMap tmB0,
+                                                           const __grid_constant__ CUtensorMap tmA1,
+                                                           const __grid_constant__ CUtensorMap tmB1, const GemmArgs g0,
+                                                           const GemmArgs g1, int* __restrict__ ready) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stA = smem;
@@ -312,8 +334,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tc::prefetch_tmap(&tmA);
-    tc::prefetch_tmap(&tmB);
+    tc::prefetch_tmap(&tmA0);
+    tc::prefetch_tmap(&tmB0);
+    tc::prefetch_tmap(&tmA1);
+    tc::prefetch_tmap(&tmB1);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, kTmemCols);
@@ -323,7 +347,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const int total = *g.nb_used * g.n_tiles;
+  const int nb = *g0.nb_used;
+  const int T0 = nb * g0.n_tiles;
+  const int total = T0 + nb * g1.n_tiles;
+  const unsigned int need = static_cast<unsigned int>(g0.n_tiles) * 4u;  // gate/up epilogue warps per block
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -332,22 +359,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-        const int blk = tile / g.n_tiles, nt = tile - blk * g.n_tiles;
+        int ph, blk, nt;
+        tile_of(tile, T0, g0, g1, ph, blk, nt);
+        const GemmArgs& g = ph ? g1 : g0;
         const int e = g.bexp[blk];
+        if (ph) {  // the block's activations are complete (all its gate/up tiles stored)
+          const unsigned int* r = reinterpret_cast<const unsigned int*>(ready + blk);
+          if (ld_acquire_u32(r) < need) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_u32(r) < need) {
+              __nanosleep(64);
+              if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                raise_error(g.ws, kErrTimeout, 0x560u);
+                ok = false;
+                break;
+              }
+            }
+            if (!ok) break;
+          }
+          fence_proxy_async_global();  // generic-proxy stores of other CTAs, read by the TMA (async proxy)
+        }
         for (int k = 0; k < g.k_steps; ++k) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, g.ws, 0x500u + KIND)) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, g.ws, 0x500u + ph)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
           uint8_t* a = stA + stage * kAStageBytes;
           uint8_t* b = stB + stage * kBStageBytes;
-          tc::tma_load_2d(a, &tmA, &full[stage], k * kBK, blk * kBM);
-          if (KIND == 0) {
-            tc::tma_load_3d(b, &tmB, &full[stage], k * kBK, nt * kGuHalf, e);
-            tc::tma_load_3d(b + kBStageBytes / 2, &tmB, &full[stage], k * kBK, g.I + nt * kGuHalf, e);
+          if (ph == 0) {
+            tc::tma_load_2d(a, &tmA0, &full[stage], k * kBK, blk * kBM);
+            tc::tma_load_3d(b, &tmB0, &full[stage], k * kBK, nt * kGuHalf, e);
+            tc::tma_load_3d(b + kBStageBytes / 2, &tmB0, &full[stage], k * kBK, g.I + nt * kGuHalf, e);
           } else {
-            tc::tma_load_3d(b, &tmB, &full[stage], k * kBK, nt * kDownN, e);
+            tc::tma_load_2d(a, &tmA1, &full[stage], k * kBK, blk * kBM);
+            tc::tma_load_3d(b, &tmB1, &full[stage], k * kBK, nt * kDownN, e);
           }
           ++issued;
           if (++stage == kStages) {
@@ -359,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       // copies still in flight land before the CTA exits (immediate when the MMA warp consumed them)
       for (int s = 0; s < kStages && s < issued; ++s) {
         const int last_round = (issued - 1 - s) / kStages;
-        mbar_wait(&full[s], static_cast<uint32_t>(last_round & 1), g.ws, 0x510u + KIND);
+        mbar_wait(&full[s], static_cast<uint32_t>(last_round & 1), g0.ws, 0x510u);
       }
     }
   } else if (warp == 1) {
@@ -370,13 +416,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++j) {
+        int ph, blk, nt;
+        tile_of(tile, T0, g0, g1, ph, blk, nt);
+        const int k_steps = ph ? g1.k_steps : g0.k_steps;
         const int buf = j & 1;
         const uint32_t aph = static_cast<uint32_t>(j >> 1) & 1u;
-        if (!mbar_wait(&acce[buf], aph ^ 1u, g.ws, 0x520u + KIND)) break;
+        if (!mbar_wait(&acce[buf], aph ^ 1u, g0.ws, 0x520u + ph)) break;
         tc::fence_after_sync();
         const uint32_t d = tmem + static_cast<uint32_t>(buf * 256);
-        for (int k = 0; k < g.k_steps; ++k) {
-          if (!mbar_wait(&full[stage], phase, g.ws, 0x530u + KIND)) {
+        for (int k = 0; k < k_steps; ++k) {
+          if (!mbar_wait(&full[stage], phase, g0.ws, 0x530u + ph)) {
             ok = false;
             break;
           }
@@ -396,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       }
       // every issued MMA retires before the TMEM is released
       tc::mma_commit(done);
-      mbar_wait(done, 0u, g.ws, 0x540u + KIND);
+      mbar_wait(done, 0u, g0.ws, 0x540u);
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
@@ -404,15 +453,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const int row = g4 * 32 + lane;
     int j = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++j) {
+      int ph, blk, nt;
+      tile_of(tile, T0, g0, g1, ph, blk, nt);
+      const GemmArgs& g = ph ? g1 : g0;
       const int buf = j & 1;
       const uint32_t aph = static_cast<uint32_t>(j >> 1) & 1u;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&accf[buf], aph, g.ws, 0x550u + KIND));
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&accf[buf], aph, g.ws, 0x550u + ph));
       if (!ok) break;
       tc::fence_after_sync();
-      const int blk = tile / g.n_tiles, nt = tile - blk * g.n_tiles;
       const long long r = static_cast<long long>(blk) * kBM + row;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(g4 * 32) << 16) + static_cast<uint32_t>(buf * 256);
-      if (KIND == 0) {
+      if (ph == 0) {
         uint4* dst = reinterpret_cast<uint4*>(g.a_out + r * g.I + nt * kGuHalf);
 #pragma unroll 1
         for (int c = 0; c < kGuHalf / 32; ++c) {
@@ -439,31 +490,38 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           for (int v = 0; v < 4; ++v)
             dst[c * 4 + v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
         }
-      } else {
-        const int p = g.sorted[r];
-        const bool live = p < g.P;
-        float w = 0.f;
-        float* dst = nullptr;
-        if (live) {
-          w = g.wts[p];
-          dst = g.y32 + static_cast<long long>(p / g.NK) * g.H + nt * kDownN;
-        }
+        tc::fence_before_sync();
+        mbar_arrive(&acce[buf]);
+        // this warp's 32 activation rows of block blk are stored: count them for the down tiles (release)
+        fence_proxy_async_global();
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(ready + blk, 1);
+        continue;
+      }
+      const int p = g.sorted[r];
+      const bool live = p < g.P;
+      float w = 0.f;
+      float* dst = nullptr;
+      if (live) {
+        w = g.wts[p];
+        dst = g.y32 + static_cast<long long>(p / g.NK) * g.H + nt * kDownN;
+      }
 #pragma unroll 1
-        for (int c = 0; c < kDownN / 32; ++c) {
-          uint32_t v[32];
-          tc::tmem_ld32(taddr + c * 32, v);
-          tc::tmem_ld_wait();
-          if (live && g.scale != nullptr) {
-            const long long sb = static_cast<long long>(g.bexp[blk]) * g.scale_se + nt * kDownN + c * 32;
+      for (int c = 0; c < kDownN / 32; ++c) {
+        uint32_t v[32];
+        tc::tmem_ld32(taddr + c * 32, v);
+        tc::tmem_ld_wait();
+        if (live && g.scale != nullptr) {
+          const long long sb = static_cast<long long>(g.bexp[blk]) * g.scale_se + nt * kDownN + c * 32;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * ld_scale(g.scale, sb + i, g.scale_bf16));
-          }
-          if (live) {
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * ld_scale(g.scale, sb + i, g.scale_bf16));
+        }
+        if (live) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              red_add_v4_f32(dst + c * 32 + 4 * i, w * __uint_as_float(v[4 * i]), w * __uint_as_float(v[4 * i + 1]),
-                             w * __uint_as_float(v[4 * i + 2]), w * __uint_as_float(v[4 * i + 3]));
-          }
+          for (int i = 0; i < 8; ++i)
+            red_add_v4_f32(dst + c * 32 + 4 * i, w * __uint_as_float(v[4 * i]), w * __uint_as_float(v[4 * i + 1]),
+                           w * __uint_as_float(v[4 * i + 2]), w * __uint_as_float(v[4 * i + 3]));
         }
       }
       tc::fence_before_sync();
@@ -483,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 struct Layout {
   int P, nb_max;
   long long rows;
-  size_t off_nb, off_align, off_sorted, off_bexp, off_xs, off_a, off_y32, off_wgu, off_wd, total;
+  size_t off_nb, off_ready, off_align, off_sorted, off_bexp, off_xs, off_a, off_y32, off_wgu, off_wd, total;
 };
 
 static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -496,6 +554,8 @@ static Layout layout(int N, int NK, int H, int I, int E1, bool int8) {
   size_t o = kWsHeaderBytes;
   L.off_nb = o;
   o += 256;
+  L.off_ready = o;  // per block: gate/up epilogue warps done (the down tiles wait for them)
+  o = up(o + static_cast<size_t>(L.nb_max) * 4, 256);
   L.off_align = o;
   o = up(o + align_scratch_bytes(L.P, E1), 256);
   L.off_sorted = o;
@@ -632,6 +692,7 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   WsHeader* hdr = reinterpret_cast<WsHeader*>(ws);
   int* nb_used = reinterpret_cast<int*>(ws + L.off_nb);
+  int* ready = reinterpret_cast<int*>(ws + L.off_ready);
   int* sorted = reinterpret_cast<int*>(ws + L.off_sorted);
   int* bexp = reinterpret_cast<int*>(ws + L.off_bexp);
   uint16_t* xs = reinterpret_cast<uint16_t*>(ws + L.off_xs);
@@ -678,7 +739,8 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
     return rc;
   const int G = num_sms();
   gather_kernel<<<G * 4, 256, 0, st>>>(static_cast<const uint16_t*>(x), x_stride, sorted, nb_used, NK, L.P, H, xs,
-                                       static_cast<const uint16_t*>(residual), residual_stride, y32, N);
+                                       static_cast<const uint16_t*>(residual), residual_stride, y32, N, ready,
+                                       L.nb_max);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, "gather launch");
   if (int8) {
@@ -701,23 +763,33 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   ga.y32 = y32;
   ga.wts = wts;
   ga.ws = hdr;
-  e = cudaFuncSetAttribute(gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kGemmSmem));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kGemmSmem));
+  e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kGemmSmem));
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm)");
+  GemmArgs g1 = ga;
   ga.n_tiles = I / kGuHalf;
   ga.k_steps = H / kBK;
   ga.scale = int8 ? w->s_gu : nullptr;
   ga.scale_se = w->sgu_se;
   ga.scale_bf16 = w->s_dtype == MV_BF16;
-  gemm_kernel<0><<<G, kThreads, kGemmSmem, st>>>(tm_xs, tm_wgu, ga);
-  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "gate/up GEMM launch");
-  ga.n_tiles = H / kDownN;
-  ga.k_steps = I / kBK;
-  ga.scale = int8 ? w->s_d : nullptr;
-  ga.scale_se = w->sd_se;
-  gemm_kernel<1><<<G, kThreads, kGemmSmem, st>>>(tm_a, tm_wd, ga);
-  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "down GEMM launch");
+  g1.n_tiles = H / kDownN;
+  g1.k_steps = I / kBK;
+  g1.scale = int8 ? w->s_d : nullptr;
+  g1.scale_se = w->sd_se;
+  g1.scale_bf16 = w->s_dtype == MV_BF16;
+  {  // cooperative: every CTA resident, so a down tile's wait for its block's gate/up tiles always ends
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kGemmSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, gemm_kernel, tm_xs, tm_wgu, tm_a, tm_wd, ga, g1, ready);
+    if (e != cudaSuccess) return cuda_status(e, "grouped GEMM launch");
+  }
   const long long n4 = static_cast<long long>(N) * H / 4;
   long long blocks = (n4 + 255) / 256;
   if (blocks > G * 8) blocks = G * 8;
