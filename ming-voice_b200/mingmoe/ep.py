@@ -8,12 +8,12 @@ replicating them costs 17 MB per expert of the 180 GB on each GPU.
 
 A prefill step on a rank's own packed tokens:
   1. RMSNorm and routing locally (mv_rmsnorm, mv_route);
-  2. every pair whose expert this rank holds (the replicated hot experts, its share of the cold ones, the
-     shared expert) is computed at once, with the residual, by one tcgen05 grouped-GEMM pass over the rank's
-     own tokens (mv_moe_prefill; the other pairs carry id -1, which the expert sort skips);
-  3. the other pairs, sorted by owner rank (stable, so every rank sends in token order): pair counts exchanged
-     with one all-to-all, then the token rows (bf16 [H]) and their metadata (slot of the expert on its owner,
-     routing weight) with all-to-all-v -- the one exchange step of the block;
+  2. the pairs whose expert lives on another rank, sorted by owner rank (stable, so every rank sends in token
+     order): pair counts exchanged with one all-to-all, then the token rows (bf16 [H]) and their metadata
+     (slot of the expert on its owner, routing weight) with all-to-all-v -- the one exchange step of the block;
+  3. while they travel, every pair whose expert this rank holds (the replicated hot experts, its share of the
+     cold ones, the shared expert) is computed by one tcgen05 grouped-GEMM pass over the rank's own tokens
+     (mv_moe_prefill; the other pairs carry id -1, which the expert sort skips);
   4. the owner computes weight * expert(row) for every received pair (mv_moe_prefill, one expert per row), the
      weighted outputs travel back (all-to-all-v, the reverse split) and are added at the origin in fp32.
 
@@ -73,10 +73,12 @@ class EPMoeBlock:
         return moe.experts(x, b.w_gu, b.w_d, ids, wts, s_gu=b.s_gu, s_d=b.s_d, residual=residual)
 
     def _local(self, xn, ids, wts, x):
-        """x + sum over this rank's pairs (ids -1 = a pair owned elsewhere, skipped) in one grouped-GEMM pass."""
+        """Sum over this rank's pairs (ids -1 = a pair owned elsewhere, skipped) in one grouped-GEMM pass, plus the
+        residual x when x is given (fused, one rounding)."""
         if self.experts_fn == self._experts_cuda:
             return self._experts_cuda(xn, ids, wts, residual=x)
-        return (x.float() + self.experts_fn(xn, ids, wts).float()).to(x.dtype)
+        y = self.experts_fn(xn, ids, wts)
+        return y if x is None else (x.float() + y.float()).to(x.dtype)
 
     def _a2a(self, out, inp, out_splits, in_splits):
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
@@ -101,13 +103,15 @@ class EPMoeBlock:
         ids_loc = torch.where(own == self.rank, slot, torch.full_like(slot, -1))
         if self.n_shared:
             ids_loc = torch.cat([ids_loc, ids[:, K:].to(ids_loc.dtype)], 1)
-        # the pairs of this rank (replicated experts, its share of the cold ones, the shared expert) and the
-        # residual: one grouped-GEMM pass over its own tokens, enqueued before the exchange's host synchronisation
-        y = self._local(xn, ids_loc.to(torch.int32).contiguous(), wts, x)
+        # the pairs of this rank (replicated experts, its share of the cold ones, the shared expert) go through
+        # one grouped-GEMM pass over its own tokens. Alone, the residual is fused into it; with remote pairs to
+        # add, the sum is completed in fp32 and rounded once.
+        ids_loc = ids_loc.to(torch.int32).contiguous()
         if self.world == 1:
-            return y
+            return self._local(xn, ids_loc, wts, x)
 
-        # the other pairs: sorted by owner (stable, so in token order per owner), exchanged, computed, returned
+        # the other pairs: sorted by owner (stable, so in token order per owner); their counts are exchanged
+        # first (the one host synchronisation of the step), so that the local pass runs while their rows travel
         flat_own = own.reshape(-1)
         key = torch.where(flat_own == self.rank, torch.full_like(flat_own, self.world), flat_own)
         order_all = torch.sort(key, stable=True).indices
@@ -115,7 +119,7 @@ class EPMoeBlock:
         recv_counts = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
         in_splits = counts.tolist()
-        out_splits = recv_counts.tolist()  # (the one host synchronisation of the step)
+        out_splits = recv_counts.tolist()
         n_send, R = sum(in_splits), sum(out_splits)
 
         order = order_all[:n_send]
@@ -125,8 +129,11 @@ class EPMoeBlock:
                                  wts[:, :K].reshape(-1)[order].to(torch.float32)], 1)
         recv_rows = torch.empty(R, H, dtype=xn.dtype, device=dev)
         recv_meta = torch.empty(R, 2, dtype=torch.float32, device=dev)
-        self._a2a(recv_rows, send_rows, out_splits, in_splits)
-        self._a2a(recv_meta, send_meta, out_splits, in_splits)
+        w_rows = dist.all_to_all_single(recv_rows, send_rows, out_splits, in_splits, group=self.group, async_op=True)
+        w_meta = dist.all_to_all_single(recv_meta, send_meta, out_splits, in_splits, group=self.group, async_op=True)
+        y_loc = self._local(xn, ids_loc, wts, None)  # overlaps the exchange
+        w_rows.wait()
+        w_meta.wait()
         if R > 0:
             lid = recv_meta[:, 0].round().to(torch.int32).unsqueeze(1)
             lw = recv_meta[:, 1].contiguous().unsqueeze(1)
@@ -135,10 +142,10 @@ class EPMoeBlock:
             y_pairs = torch.empty(0, H, dtype=xn.dtype, device=dev)
         back = torch.empty(n_send, H, dtype=y_pairs.dtype, device=dev)
         self._a2a(back, y_pairs.contiguous(), in_splits, out_splits)
-        if n_send == 0:
-            return y
-        y32 = y.to(torch.float32)
-        y32.index_add_(0, tok, back.to(torch.float32))
+        y32 = x.to(torch.float32, copy=True)  # (never an alias of the caller's tokens)
+        y32 += y_loc.to(torch.float32)
+        if n_send:
+            y32.index_add_(0, tok, back.to(torch.float32))
         return y32.to(x.dtype)
 
 
