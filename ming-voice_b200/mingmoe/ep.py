@@ -11,11 +11,11 @@ A prefill step on a rank's own packed tokens:
   2. the pairs whose expert lives on another rank, sorted by owner rank (stable, so every rank sends in token
      order): pair counts exchanged with one all-to-all, then the token rows (bf16 [H]) and their metadata
      (slot of the expert on its owner, routing weight) with all-to-all-v -- the one exchange step of the block;
-  3. while they travel, every pair whose expert this rank holds (the replicated hot experts, its share of the
-     cold ones, the shared expert) is computed by one tcgen05 grouped-GEMM pass over the rank's own tokens
-     (mv_moe_prefill; the other pairs carry id -1, which the expert sort skips);
-  4. the owner computes weight * expert(row) for every received pair (mv_moe_prefill, one expert per row), the
-     weighted outputs travel back (all-to-all-v, the reverse split) and are added at the origin in fp32.
+  3. ONE tcgen05 grouped-GEMM pass (mv_moe_prefill) over the rank's own tokens and the received rows: an own
+     token carries the pairs whose expert this rank holds (the replicated hot experts, its share of the cold
+     ones, the shared expert; the other pairs -1, which the expert sort skips), a received row its one pair;
+  4. the received rows' weighted outputs travel back (all-to-all-v, the reverse split) and are added at the
+     origin in fp32 with the residual and the local output, rounded once.
 
 The exchange sizes are data dependent, so a step synchronises the host once (the split sizes); prefill is not
 graph-captured. No kernel reads another GPU's memory: everything remote arrives through NCCL.
@@ -111,7 +111,7 @@ class EPMoeBlock:
             return self._local(xn, ids_loc, wts, x)
 
         # the other pairs: sorted by owner (stable, so in token order per owner); their counts are exchanged
-        # first (the one host synchronisation of the step), so that the local pass runs while their rows travel
+        # first (the one host synchronisation of the step), then their rows and metadata
         flat_own = own.reshape(-1)
         key = torch.where(flat_own == self.rank, torch.full_like(flat_own, self.world), flat_own)
         order_all = torch.sort(key, stable=True).indices
@@ -129,21 +129,22 @@ class EPMoeBlock:
                                  wts[:, :K].reshape(-1)[order].to(torch.float32)], 1)
         recv_rows = torch.empty(R, H, dtype=xn.dtype, device=dev)
         recv_meta = torch.empty(R, 2, dtype=torch.float32, device=dev)
-        w_rows = dist.all_to_all_single(recv_rows, send_rows, out_splits, in_splits, group=self.group, async_op=True)
-        w_meta = dist.all_to_all_single(recv_meta, send_meta, out_splits, in_splits, group=self.group, async_op=True)
-        y_loc = self._local(xn, ids_loc, wts, None)  # overlaps the exchange
-        w_rows.wait()
-        w_meta.wait()
+        self._a2a(recv_rows, send_rows, out_splits, in_splits)
+        self._a2a(recv_meta, send_meta, out_splits, in_splits)
+        # one grouped-GEMM pass over this rank's own tokens and the received rows together: own rows carry their
+        # local pairs (others -1), a received row its one (slot, weight) pair in column 0 and -1 elsewhere
+        NK = ids_loc.shape[1]
+        r_ids = torch.full((R, NK), -1, dtype=torch.int32, device=dev)
+        r_wts = torch.zeros(R, NK, dtype=torch.float32, device=dev)
         if R > 0:
-            lid = recv_meta[:, 0].round().to(torch.int32).unsqueeze(1)
-            lw = recv_meta[:, 1].contiguous().unsqueeze(1)
-            y_pairs = self.experts_fn(recv_rows, lid, lw)
-        else:
-            y_pairs = torch.empty(0, H, dtype=xn.dtype, device=dev)
-        back = torch.empty(n_send, H, dtype=y_pairs.dtype, device=dev)
-        self._a2a(back, y_pairs.contiguous(), in_splits, out_splits)
+            r_ids[:, 0] = recv_meta[:, 0].round().to(torch.int32)
+            r_wts[:, 0] = recv_meta[:, 1]
+        y_all = self._local(torch.cat([xn, recv_rows]), torch.cat([ids_loc, r_ids]),
+                            torch.cat([wts.to(torch.float32), r_wts]), None)
+        back = torch.empty(n_send, H, dtype=y_all.dtype, device=dev)
+        self._a2a(back, y_all[N:].contiguous(), in_splits, out_splits)
         y32 = x.to(torch.float32, copy=True)  # (never an alias of the caller's tokens)
-        y32 += y_loc.to(torch.float32)
+        y32 += y_all[:N].to(torch.float32)
         if n_send:
             y32.index_add_(0, tok, back.to(torch.float32))
         return y32.to(x.dtype)
