@@ -115,7 +115,9 @@ class EPMoeBlock:
         flat_own = own.reshape(-1)
         key = torch.where(flat_own == self.rank, torch.full_like(flat_own, self.world), flat_own)
         order_all = torch.sort(key, stable=True).indices
-        counts = torch.bincount(key, minlength=self.world + 1)[: self.world].contiguous()
+        # (index_add, not bincount: bincount sizes its output from the data, a host synchronisation on CUDA)
+        counts = torch.zeros(self.world + 1, dtype=torch.long, device=dev).index_add_(0, key, torch.ones_like(key))
+        counts = counts[: self.world].contiguous()
         recv_counts = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
         in_splits = counts.tolist()
