@@ -12,7 +12,11 @@ whole-job time per block-token (lower is better; N > 1 runs independent replicas
 
 Keys beyond the base contract: roofline (HBM, measured copy peak), cpu_baseline (the oracle's torch-eager
 fp32 block on the host cores), e2e (the same metric through the public MoeBlock.decode API with the token
-copied host->device and the result device->host every step), gpu_launches, clocks.
+copied host->device and the result device->host every step), gpu_launches, clocks; prefill (BASELINE
+the 2043-token ragged pass in a CUDA graph on one GPU, expert parallel over N > 1 ranks) with its
+tensor roofline; int8_decode (BASELINE configs[2] at M=1 through the same 16-layer graph chain, one GPU) with
+its HBM roofline. --decode-m M measures the other configs[1] token counts, --prefill-only the prefill pass
+alone, --no-prefill / --no-int8 skip those parts.
 """
 from __future__ import annotations
 
