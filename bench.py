@@ -137,6 +137,8 @@ def make_stack(device, layers, seed=3, int8=False):
                                    s_gu=s_gu, s_d=s_d, router_s=s_rw))
         else:
             blocks.append(MoeBlock(w_gu, w_d, rw, nw, top_k=TOPK, shared_ids=tuple(range(E, E1)), eps=1e-6))
+    for layer, blk in enumerate(blocks):  # block l prefetches the routing weights of block l + 1 (a step repeats)
+        blk.link(blocks[(layer + 1) % len(blocks)])
     return blocks
 
 
@@ -187,7 +189,7 @@ def int8_decode_lines(dev, steps, warmup, layers=16, Md=1):
 
 
 def cpu_block_time_us(reps=5):
-    """The oracle's torch-eager fp32 block (BASELINE.md section 3) on the host cores: us per block-token at M=1."""
+    """The oracle's torch-eager fp32 block on the host cores: us per block-token at M=1."""
     from oracle import moe_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
     p = O.make_block_params(seed=3, dtype=torch.float32)

@@ -94,6 +94,18 @@ MV_API size_t mv_route_workspace_bytes(int n_tokens, int E);
 MV_API int mv_quantize_rows_int8(const void* w, int w_dtype, long long w_stride, long long rows, int K, int8_t* q,
                           void* scale, int scale_dtype, void* stream);
 
+/* Quantise-on-load into a stacked slot: replaces the loader hook of ming-voice's _int8_expert_loaders
+ * (engine.py:126-147: quantize_rows_int8 on the device, then copies into q[e, off:off + n] and s[e, off:off + n]),
+ * which the loader threads call per checkpoint tensor (direct_load.py:109-135). The `rows` x K matrix w (row
+ * stride w_stride elements; bf16/f16/f32; device memory or pinned host memory the device can read) is quantised
+ * as mv_quantize_rows_int8 does and written directly to rows [row_off, row_off + rows) of slot e of the
+ * contiguous int8 stack q_stack [E1, rows_per_expert, K] and of the scale stack s_stack [E1, rows_per_expert]
+ * (s_dtype f32 or bf16). Nothing is allocated; calls on different streams for different slots may run at the
+ * same time (each loader thread on its own stream). */
+MV_API int mv_quantize_into_stack(const void* w, int w_dtype, long long w_stride, int rows, int K, int8_t* q_stack,
+                                  void* s_stack, int s_dtype, int E1, int rows_per_expert, int e, int row_off,
+                                  void* stream);
+
 /* Dequantisation exactly as the int8 kernels perform it in registers: out = float(q) * float(scale[row]),
  * one correctly rounded fp32 multiply (== torch q.float() * s.float()). Exported so the in-kernel
  * dequantisation can be checked bit for bit. q: rows x K contiguous; out: rows x K f32. */
@@ -202,6 +214,9 @@ typedef struct mv_block {
   int residual_from_x;      /* 1: out = x + MoE(norm(x)) (the decoder layer's residual); 0: out = MoE(...) */
   int pad0;
   double route_scale;       /* sigmoid mode: routed_scaling_factor */
+  const struct mv_block* next; /* the block decoded after this one, or NULL. Decode only reads its router weight
+                                  and RMSNorm weight pointers: they are prefetched into L2 while this block runs,
+                                  so the next block's routing starts from L2 (a layer stack links block l to l+1). */
 } mv_block;
 
 /* Decode step of one block for M <= 16 tokens in ONE cooperative kernel: replaces the patched single-token
@@ -216,12 +231,21 @@ MV_API size_t mv_block_decode_workspace_bytes(int M, int n_experts_per_token, in
 /* Workspace for the fastest mv_block_decode path for up to M tokens (see mv_moe_decode_workspace_bytes_tc). */
 MV_API size_t mv_block_decode_workspace_bytes_tc(const mv_block* b, int M);
 
+/* Padded-bucket prefill: sets ids[r, k] = -1 ("no pair", skipped by mv_moe_prefill) for every row
+ * r >= *n_valid of the [N, NK] expert ids (i32 or i64). n_valid is a device int read by the kernel, so a CUDA
+ * graph captured once for a padded length N serves every prompt length up to N: ming-voice pads short prompts
+ * to 32 / 64 / 128 tokens and replays one graph per length (engine.py:716-757, :950-961), where the padded rows
+ * also run through the experts; here they are dropped from the expert sort. */
+MV_API int mv_mask_pad_rows(void* ids, int ids_dtype, int N, int NK, const int* n_valid, void* stream);
+
 /* mv_block_decode without a caller workspace: no counterpart in the reference (its Triton launches take
  * torch-allocated buffers). For callers that cannot allocate device memory or keep a workspace -- a C/FFI
  * host without a device allocator, or code that must not call cudaMalloc while a stream is captured.
  * The scratch is a static 1 MiB device array per device; the first call on a device (with it current)
  * looks its address up, so make that call before any stream capture. Calls whose scratch need
- * (mv_block_decode_workspace_bytes) exceeds 1 MiB are rejected with MV_ERR_WORKSPACE. Each call clears the
+ * (mv_block_decode_workspace_bytes) exceeds 1 MiB are rejected with MV_ERR_WORKSPACE. Every call runs the
+ * CUDA-core decode kernel: the tensor-core kernel's layout (3.4 MB at M = 1 up to 50 MB at M = 16 for H=2048,
+ * I=1408, 64 + 2 slots) does not fit the static scratch. Each call clears the
  * scratch's 256-byte header (barrier counters, error word) on `stream` before its launch.
  * status_out (device or pinned host memory, 2 x u32, may be NULL) receives the call's device-side error
  * code and location, as mv_workspace_status reports them. One scratch per device: calls that can run

@@ -72,7 +72,26 @@ struct Params {
   float* tc_part_d;    // [G * kTcMaxSeg][M][128] down-projection pieces
   uint16_t* tc_abuf;   // [u_max * 32][I] bf16: rows 0..15 = hi(a * w) per token, 16..31 = lo
   int* tc_cnt;         // [(u_max * (I / 128) + H / 128) * 4] arrival counters per 32-row group (zero between calls)
+  // next-block L2 prefetch (decode kernels)
+  const uint8_t* nx_rw;      // the next block's router weight (NULL: no next block) ...
+  long long nx_rw_bytes;     // ... its size in bytes (a multiple of 16)
+  const uint16_t* nx_norm;   // the next block's RMSNorm weight [H] bf16, or NULL
+#ifdef MV_TRACE
+  unsigned long long* trace;  // [G][32] %globaltimer stamps per CTA (phase-timing builds only)
+#endif
 };
+
+// Phase timestamps for timing studies: compiled only with -DMV_TRACE (a separate build); nothing otherwise.
+#ifdef MV_TRACE
+#define MV_TRACE_AT(p, k)                                                                   \
+  do {                                                                                      \
+    if ((p).trace != nullptr) (p).trace[blockIdx.x * 32 + (k)] = globaltimer_ns();          \
+  } while (0)
+#else
+#define MV_TRACE_AT(p, k) \
+  do {                    \
+  } while (0)
+#endif
 
 constexpr int kTcMaxSeg = 4;
 
@@ -104,6 +123,104 @@ struct GuWalk {
     return true;
   }
 };
+
+// The ring stages of a gate/up walk in order: each segment of the walk cut into stages of RG rows (gate rows
+// [i, i + nr) and the matching up rows). The producer's copies, its L2 lookahead and the consumers all follow
+// this one sequence.
+struct GuStages {
+  GuWalk w;
+  int u = 0, i0 = 0, ni = 0, s0 = 0;
+  __device__ bool next(int& uu, int& i, int& nr, int RG) {
+    if (s0 >= ni) {
+      long long r0w;
+      if (!w.next(u, i0, ni, r0w)) return false;
+      s0 = 0;
+    }
+    uu = u;
+    i = i0 + s0;
+    nr = min(RG, ni - s0);
+    s0 += RG;
+    return true;
+  }
+};
+
+// The ring stages of the down projection: the (expert u, output row r) entries of a CTA in order, `per` entries
+// per stage, a stage either crossing expert boundaries (packed) or ending at them. next() calls f(u, r, n, k) for
+// each run of rows of one expert in the stage (k = the run's first entry within the stage).
+struct DownStages {
+  int u = 0, r = 0;
+  template <class F>
+  __device__ bool next(int U, int nh, int per, bool cross, F&& f) {
+    if (u >= U || nh <= 0) return false;
+    int left = per, k = 0;
+    while (left > 0 && u < U) {
+      const int n = min(left, nh - r);
+      f(u, r, n, k);
+      left -= n;
+      r += n;
+      k += n;
+      if (r == nh) {
+        r = 0;
+        ++u;
+        if (!cross) break;
+      }
+    }
+    return true;
+  }
+  // entries in the next stage (0 at the end)
+  __device__ int entries(int U, int nh, int per, bool cross) const {
+    if (u >= U || nh <= 0) return 0;
+    return cross ? min(per, (U - u) * nh - r) : min(per, nh - r);
+  }
+};
+
+// Sums each of the 8 values v[0..7] over the 32 lanes of the warp in a fixed order; afterwards v[0] of lane l holds
+// the sum of value (l >> 2) & 7. Three exchanges that halve the values held (4, 2, 1 shuffles), then two butterfly
+// steps: 9 shuffles for 8 sums instead of 40.
+__device__ __forceinline__ void reduce8(float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+  const bool b4 = (lane & 16) != 0, b3 = (lane & 8) != 0, b2 = (lane & 4) != 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = b4 ? v[i] : v[i + 4];
+    const float keep = b4 ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b3 ? v[i] : v[i + 2];
+    const float keep = b3 ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const float send = b2 ? v[0] : v[1];
+    const float keep = b2 ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+// a{0,1} += the dot of one 16-byte weight chunk (VEC elements in order; int8 dequantised element by element as
+// float(q) * sc) with xv[0..VEC): even elements into a0, odd into a1 (packed fp32 FMAs).
+template <bool INT8>
+__device__ __forceinline__ void chunk_fma(float& a0, float& a1, const uint4& wv, const float* xv, float sc) {
+  const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+  if (INT8) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float f0, f1, f2, f3;
+      i8x4_to_f32(w[q], f0, f1, f2, f3);
+      fmul2(f0, f1, f0, f1, sc);
+      fmul2(f2, f3, f2, f3, sc);
+      ffma2(a0, a1, f0, f1, xv[4 * q], xv[4 * q + 1]);
+      ffma2(a0, a1, f2, f3, xv[4 * q + 2], xv[4 * q + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ffma2(a0, a1, bf16lo(w[q]), bf16hi(w[q]), xv[2 * q], xv[2 * q + 1]);
+  }
+}
 
 __device__ __forceinline__ float ldscale(const void* base, long long idx, int bf16) {
   if (bf16) return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(base)[idx]) << 16);
@@ -261,6 +378,8 @@ __device__ void table_bitmap(const int* pr_e, const float* pr_w, int npairs, int
 // The tensor-core decode path (bf16 weights): workspace need and launch. Returns MV_OK, an error, or
 // kDecodeTcUnsuitable when the shapes / workspace do not fit it (the caller then uses the CUDA-core kernel).
 constexpr int kDecodeTcUnsuitable = -1;
+constexpr int kDecodeM1Unsuitable = -2;
+int decode_m1_run(decode::Params& p, bool int8, cudaStream_t st);
 size_t decode_tc_workspace_bytes(int M, int nk, int H, int I, int E1, int E, int n_static);
 int decode_tc_run(decode::Params& p, void* workspace, size_t workspace_bytes, int nk_pairs, cudaStream_t st);
 

@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
         const bool valid = e >= 0 && e < p.E1;
         pr_e[j] = valid ? static_cast<int>(e) : -1;
         pr_w[j] = p.wts[j];
-        if (!valid) raise_error(p.ws, kErrBadExpert, static_cast<unsigned int>(j));
+        if (!valid && e != -1) raise_error(p.ws, kErrBadExpert, static_cast<unsigned int>(j));  // -1: no pair
       }
       __syncwarp();
       if (npairs <= 32)
@@ -888,6 +888,13 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
   const size_t lg = (static_cast<size_t>(M) * (p.router ? p.E : 0) * 4 + 255) & ~size_t(255);
   p.logits_ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes);
   p.a_g = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes + lg);
+  {  // one token with the router fused: the dedicated kernel (moe_decode_m1.cu) when MINGMOE_DECODE_PATH=m1
+    const char* path = getenv("MINGMOE_DECODE_PATH");
+    if (M == 1 && p.router && path != nullptr && path[0] == 'm') {
+      const int rc = decode_m1_run(p, int8, st);
+      if (rc != kDecodeM1Unsuitable) return rc;
+    }
+  }
   p.RG = RG;
   p.DR = DR;
   p.DP = DR;
@@ -1063,6 +1070,17 @@ extern "C" int mv_block_decode(const mv_block* b, const void* x, int M, void* ou
   p.wts_out = wts_out;
   p.residual = b->residual_from_x ? static_cast<const uint16_t*>(x) : nullptr;
   p.out = static_cast<uint16_t*>(out);
+  if (b->next != nullptr && b->next->router_w != nullptr && aligned16(b->next->router_w)) {
+    const mv_block* n = b->next;
+    const int resz = n->router_dtype == MV_F32 ? 4 : (n->router_dtype == MV_BF16 ? 2 : 1);
+    const long long bytes = static_cast<long long>(n->E) * n->experts.H * resz;
+    if (bytes > 0 && bytes % 16 == 0) {
+      p.nx_rw = static_cast<const uint8_t*>(n->router_w);
+      p.nx_rw_bytes = bytes;
+      if (n->norm_w != nullptr && aligned16(n->norm_w) && n->experts.H == b->experts.H)
+        p.nx_norm = static_cast<const uint16_t*>(n->norm_w);
+    }
+  }
   return decode_run(p, &b->experts, workspace, workspace_bytes, b->top_k + b->n_shared,
                     static_cast<cudaStream_t>(stream));
 }

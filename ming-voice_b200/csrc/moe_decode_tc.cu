@@ -594,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool valid = e >= 0 && e < p.E1;
         pr_e[j] = valid ? static_cast<int>(e) : -1;
         pr_w[j] = p.wts[j];
-        if (!valid) raise_error(p.ws, kErrBadExpert, static_cast<unsigned int>(j));
+        if (!valid && e != -1) raise_error(p.ws, kErrBadExpert, static_cast<unsigned int>(j));  // -1: no pair
       }
       rbar();
       if (npairs <= 32) {

@@ -9,7 +9,6 @@ save_cache() has nothing to save and small_linear never raises for an untuned sh
 from __future__ import annotations
 
 import ctypes as C
-import time
 
 import torch
 
@@ -22,25 +21,26 @@ def save_cache():
 
 
 def _graph_time(fn, reps=20, inner=40):
-    """Seconds per call of fn, measured over CUDA-graph replays of `inner` back-to-back calls (the reference's
-    timing helper, fastlinear.py:105-122)."""
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        fn()
-        s.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=s):
+    """Seconds per call of fn (same name and arguments as the reference's helper, fastlinear.py:105-122, which
+    dev/mm_compare.py imports). One CUDA graph holds `inner` calls; after one warm replay, `reps` replays are
+    bracketed by CUDA events on the replay stream, so the figure is device time without host launch cost."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        fn()  # creates any lazily built state (workspaces) outside the capture
+        with torch.cuda.graph(graph, stream=side):
             for _ in range(inner):
                 fn()
-        g.replay()
-        s.synchronize()
-        t = time.perf_counter()
+        graph.replay()
+        begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        begin.record(side)
         for _ in range(reps):
-            g.replay()
-        s.synchronize()
-    torch.cuda.current_stream().wait_stream(s)
-    return (time.perf_counter() - t) / reps / inner
+            graph.replay()
+        end.record(side)
+    end.synchronize()
+    torch.cuda.current_stream().wait_stream(side)
+    return begin.elapsed_time(end) * 1e-3 / (reps * inner)
 
 
 def small_linear(x, w, b=None, act=0, residual=None, out=None, norm=None):

@@ -42,7 +42,7 @@ class Block(C.Structure):
     _fields_ = [("experts", MoeWeights), ("norm_w", P), ("router_w", P), ("router_scale", P), ("router_bias", P),
                 ("eps", F32), ("router_dtype", I32), ("router_scale_dtype", I32), ("E", I32), ("top_k", I32),
                 ("route_mode", I32), ("n_group", I32), ("topk_group", I32), ("n_shared", I32), ("shared_id", I32),
-                ("residual_from_x", I32), ("pad0", I32), ("route_scale", F64)]
+                ("residual_from_x", I32), ("pad0", I32), ("route_scale", F64), ("next", P)]
 
 
 _SIGS = {
@@ -67,6 +67,8 @@ _SIGS = {
     "mv_moe_align_workspace_bytes": (SZ, [I32, I32]),
     "mv_moe_prefill": (I32, [C.POINTER(MoeWeights), P, I64, P, I32, P, I32, I32, P, I64, P, P, SZ, P]),
     "mv_moe_prefill_workspace_bytes": (SZ, [I32, I32, I32, I32, I32, I32]),
+    "mv_quantize_into_stack": (I32, [P, I32, I64, I32, I32, P, P, I32, I32, I32, I32, I32, P]),
+    "mv_mask_pad_rows": (I32, [P, I32, I32, I32, P, P]),
 }
 
 _lib = None
@@ -127,11 +129,16 @@ def require_cuda(*tensors):
 # ---------------------------------------------------------------------------------------------- workspaces
 
 _ws: dict = {}
+# Workspaces replaced by a larger one. A CUDA graph captured while one of them was current keeps its address
+# and writes to it on every replay, so a superseded buffer is never returned to the allocator: it stays alive
+# (and is still checked by all_workspace_errors) for the life of the process.
+_retired: list = []
 
 
 def workspace(kind: str, nbytes: int, device: torch.device) -> torch.Tensor:
     """A zero-initialised uint8 device buffer of >= nbytes reused by every call of `kind` on the current
-    stream (the kernels leave it zeroed). Creating or growing one is not allowed during stream capture."""
+    stream (the kernels leave it zeroed). Creating or growing one is not allowed during stream capture; a buffer
+    outgrown by a later eager call is kept alive, not freed, because a captured graph may still use it."""
     stream = torch.cuda.current_stream(device)
     key = (kind, device.index if device.index is not None else torch.cuda.current_device(), stream.cuda_stream)
     buf = _ws.get(key)
@@ -140,6 +147,9 @@ def workspace(kind: str, nbytes: int, device: torch.device) -> torch.Tensor:
             raise RuntimeError(f"mingmoe workspace '{kind}' ({nbytes} bytes) must be created before graph capture; "
                                "run the call once eagerly first")
         nb = max(nbytes, 1 << 16)
+        if buf is not None:
+            nb = max(nb, 2 * buf.numel())  # geometric growth: few superseded buffers stay alive
+            _retired.append((key, buf))
         buf = torch.zeros(nb, dtype=torch.uint8, device=device)
         _ws[key] = buf
     return buf
@@ -155,7 +165,7 @@ def workspace_status(buf: torch.Tensor, clear=True):
 def all_workspace_errors(clear=True):
     """Device-side error words of every cached workspace: {(kind, device, stream): (code, info)} for non-zero."""
     out = {}
-    for k, buf in list(_ws.items()):
+    for k, buf in list(_ws.items()) + [((*k, "retired", n), b) for n, (k, b) in enumerate(_retired)]:
         c, i = workspace_status(buf, clear)
         if c:
             out[k] = (c, i)

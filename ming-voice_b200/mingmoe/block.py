@@ -62,6 +62,7 @@ class MoeBlock:
         b.shared_id = shared_ids[0] if shared_ids else 0
         b.residual_from_x = 1
         self._block = b
+        self._next = None
         self.nk = self.top_k + len(shared_ids)
 
     @classmethod
@@ -72,6 +73,14 @@ class MoeBlock:
                    eps=p["eps"], s_gu=g.get("s_gu"), s_d=g.get("s_d"), router_s=g.get("router_s"),
                    router_bias=None if router_bias is None else router_bias.to(device), route_mode=route_mode,
                    n_group=p.get("n_group", 1), topk_group=p.get("topk_group", 1), route_scale=p.get("scale", 1.0))
+
+    def link(self, nxt):
+        """Declare the block decoded after this one (None to unlink). While this block's decode kernel runs it
+        prefetches the next block's router and RMSNorm weights into L2, so the next block's routing starts from L2.
+        A layer stack links block l to block l + 1 (and the last to the first when steps repeat)."""
+        self._next = nxt
+        self._block.next = None if nxt is None else C.addressof(nxt._block)
+        return self
 
     # ------------------------------------------------------------------------------------------ decode
     def workspace_bytes(self, M=moe.DECODE_MAX_M):
@@ -109,11 +118,18 @@ class MoeBlock:
                             shared_id=self.shared_ids[0] if self.shared_ids else self.E, w_scale=self.router_s)
         return ids, wts, logits
 
-    def prefill(self, x):
-        """h + MoE(rms_norm(h)) for N packed tokens (any N; sequences are independent per token)."""
+    def prefill(self, x, n_valid=None):
+        """h + MoE(rms_norm(h)) for N packed tokens (any N; sequences are independent per token).
+
+        n_valid: optional device int32 [1]; rows >= n_valid[0] are padding (a prompt padded to a bucket length
+        whose graph was captured once): their expert pairs are dropped (mv_mask_pad_rows) and they come out as
+        their input."""
         import fused_ops
         x2 = x.reshape(-1, self.H)
         xn = fused_ops.rms_norm(x2, self.norm_w, self.eps) if self.norm_w is not None else x2
         ids, wts, _ = self.route(xn)
+        if n_valid is not None:
+            L.check(L.lib().mv_mask_pad_rows(L.ptr(ids), L.dt(ids), ids.shape[0], ids.shape[1], L.ptr(n_valid),
+                                             L.stream_ptr(x.device)), "mv_mask_pad_rows")
         y = moe.experts(xn, self.w_gu, self.w_d, ids, wts, s_gu=self.s_gu, s_d=self.s_d, residual=x2)
         return y.view(x.shape)

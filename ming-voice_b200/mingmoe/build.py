@@ -40,12 +40,12 @@ def _deps():
                   glob.glob(os.path.join(INCLUDE, "*.h")))
 
 
-def _compile(src: str, verbose: bool, ptxas_v: bool) -> str:
-    obj = os.path.join(BUILD, os.path.basename(src) + ".o")
+def _compile(src: str, verbose: bool, ptxas_v: bool, build_dir: str = BUILD, extra=()) -> str:
+    obj = os.path.join(build_dir, os.path.basename(src) + ".o")
     newest_dep = max([os.path.getmtime(src)] + [os.path.getmtime(d) for d in _deps()])
     if os.path.exists(obj) and os.path.getmtime(obj) >= newest_dep and not ptxas_v:
         return obj
-    cmd = [nvcc(), *ARCH, *FLAGS, "-c", src, "-o", obj]
+    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-c", src, "-o", obj]
     if ptxas_v:
         cmd += ["-Xptxas", "-v"]
     if verbose:
@@ -58,14 +58,18 @@ def _compile(src: str, verbose: bool, ptxas_v: bool) -> str:
     return obj
 
 
-def build(verbose: bool = False, force: bool = False, ptxas_v: bool = False) -> str:
-    os.makedirs(BUILD, exist_ok=True)
+def build(verbose: bool = False, force: bool = False, ptxas_v: bool = False, out: str = OUT, build_dir: str = BUILD,
+          extra=()) -> str:
+    """Compile and link; `out`, `build_dir` and `extra` nvcc flags select a variant build (e.g. -DMV_TRACE for
+    the phase-timing stamps of the decode kernel) without touching the default library."""
+    OUT = out
+    os.makedirs(build_dir, exist_ok=True)
     if force:
-        for f in glob.glob(os.path.join(BUILD, "*.o")):
+        for f in glob.glob(os.path.join(build_dir, "*.o")):
             os.remove(f)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose, ptxas_v), srcs))
+        objs = list(ex.map(lambda s: _compile(s, verbose, ptxas_v, build_dir, tuple(extra)), srcs))
     if (not os.path.exists(OUT) or force or ptxas_v or
             max(os.path.getmtime(o) for o in objs) > os.path.getmtime(OUT)):
         tmp = OUT + ".tmp"

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference sources (read-only) and Triton:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py <path of the ming-voice sources>
 
 It imports the reference's `fused_moe.py`, `fused_ops.py` and `fastlinear.py` with TRITON_INTERPRET=1, so the
 reference Triton kernels execute on the CPU, feeds them small seeded inputs and saves inputs + outputs to
@@ -25,7 +25,9 @@ import os
 import sys
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) != 2:
+    sys.exit("usage: python tests/golden/make_golden.py <path of the ming-voice sources>")
+REF = sys.argv[1]
 sys.path.insert(0, REF)
 HERE = os.path.dirname(os.path.abspath(__file__))
 

@@ -234,3 +234,26 @@ def test_decode_tensor_core_and_cuda_core_paths_agree(cuda, base_params, M):
     close(y_cc, y_ref)
     close(y_tc, y_cc.float(), max_abs=1.6e-2)
     no_device_errors()
+
+
+@pytest.mark.parametrize("M", [1, 3, 16])
+def test_decode_skips_pairs_marked_minus_one(cuda, base_params, base_params_gpu, M):
+    """Expert-parallel prefill marks the pairs held by another rank with id -1; with <= 16 tokens they reach the
+    decode kernels, which skip them without flagging an error (an id outside [0, E1) other than -1 is flagged)."""
+    p, pg = base_params, base_params_gpu
+    x = O.make_tokens(M, seed=9)
+    xn = O.rms_norm(x, p["norm_w"], p["eps"])
+    ids, wts, _ = O.route_softmax(xn, p["router_w"], top_k=6, shared_ids=p["shared_ids"])
+    ids = ids.clone()
+    ids[:, 1::2] = -1  # every other pair lives elsewhere
+    ref = O.moe_experts(xn, p["w_gu"], p["w_d"], torch.where(ids < 0, 0, ids), torch.where(ids < 0, 0.0, wts))
+    L.all_workspace_errors(clear=True)
+    for path in ("c", "tc"):
+        import os
+        os.environ["MINGMOE_DECODE_PATH"] = path
+        try:
+            got = moe.experts(xn.to(cuda), pg["w_gu"], pg["w_d"], ids.to(cuda).to(torch.int32), wts.to(cuda))
+        finally:
+            del os.environ["MINGMOE_DECODE_PATH"]
+        close(got, ref)
+        no_device_errors()

@@ -44,6 +44,30 @@ def test_noalloc_matches_workspace_entry_point(cuda, M):
         assert status.tolist() == [0, 0]
 
 
+def test_noalloc_alternating_token_counts(cuda):
+    """Calls with different M in a row on one stream: each finds the shared scratch as a call of another token
+    count (another instance of the CUDA-core kernel: 1, up to 4 or up to 16 tokens) left it. Within the 1 MiB
+    scratch every call runs the CUDA-core kernel; the reference calls below, with a full workspace, run the
+    tensor-core kernel from M = 2, so the two agree within the tolerance, not bit for bit."""
+    p = O.make_block_params(seed=0)
+    blk = MoeBlock.from_params(p)
+    for M in (16, 1, 4, 1, 2, 16, 8, 1):
+        x = O.make_tokens(M, seed=30 + M).to(cuda)
+        ids_ref = torch.empty(M, 8, dtype=torch.long, device=cuda)
+        y_ref = blk.decode(x, ids=ids_ref)
+        out = torch.empty_like(x)
+        ids = torch.full((M, 8), -1, dtype=torch.long, device=cuda)
+        wts = torch.zeros(M, 8, device=cuda)
+        status = torch.full((2,), 7, dtype=torch.int32, device=cuda)
+        assert call_noalloc(blk, x, out, ids, wts, status) == 0, L.lib().mv_last_error().decode()
+        torch.cuda.synchronize()
+        assert torch.equal(ids, ids_ref), M
+        d = (out.float() - y_ref.float()).abs()
+        assert d.max().item() <= MAX_ABS
+        assert (d.sum() / y_ref.float().abs().sum()).item() <= MEAN_REL
+        assert status.tolist() == [0, 0], M
+
+
 def test_noalloc_rejects_scratch_beyond_its_size(cuda):
     b = L.Block()
     b.E, b.top_k, b.n_shared = 64, 6, 2
