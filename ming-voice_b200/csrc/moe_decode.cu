@@ -823,6 +823,10 @@ using decode::Params;
 // MINGMOE_DECODE_PATH=classic / =tc forces either kernel.
 constexpr int kTcMinM = 2;
 
+#ifdef MV_TRACE
+void* g_decode_trace = nullptr;  // phase-timing builds: [G][32] u64 stamps of the next launches
+#endif
+
 // Geometry, validation and the cooperative launch; shared by mv_moe_decode and mv_block_decode.
 int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t workspace_bytes, int nk_pairs,
                cudaStream_t st) {
@@ -877,6 +881,9 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
   p.I = I;
   p.s_bf16 = w->s_dtype == MV_BF16;
   p.ws = static_cast<WsHeader*>(workspace);
+#ifdef MV_TRACE
+  p.trace = static_cast<unsigned long long*>(g_decode_trace);
+#endif
   if (!int8) {  // the tensor-core kernel when the shapes and the workspace suit it (M >= kTcMinM)
     const char* path = getenv("MINGMOE_DECODE_PATH");
     const bool force_tc = path != nullptr && path[0] == 't';
@@ -888,9 +895,12 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
   const size_t lg = (static_cast<size_t>(M) * (p.router ? p.E : 0) * 4 + 255) & ~size_t(255);
   p.logits_ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes);
   p.a_g = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes + lg);
-  {  // one token with the router fused: the dedicated kernel (moe_decode_m1.cu) when MINGMOE_DECODE_PATH=m1
+  {  // one token with the router fused, int8 weights: the dedicated kernel (moe_decode_m1.cu: 42.6 vs 44.0 us per
+    // block in the 16-layer graph; for bf16 this kernel measured 48.8 us against 44.9, so bf16 runs it only with
+    // MINGMOE_DECODE_PATH=m1, and =classic keeps int8 here too)
     const char* path = getenv("MINGMOE_DECODE_PATH");
-    if (M == 1 && p.router && path != nullptr && path[0] == 'm') {
+    const bool want = path != nullptr ? path[0] == 'm' : int8;
+    if (M == 1 && p.router && want) {
       const int rc = decode_m1_run(p, int8, st);
       if (rc != kDecodeM1Unsuitable) return rc;
     }
@@ -1084,3 +1094,7 @@ extern "C" int mv_block_decode(const mv_block* b, const void* x, int M, void* ou
   return decode_run(p, &b->experts, workspace, workspace_bytes, b->top_k + b->n_shared,
                     static_cast<cudaStream_t>(stream));
 }
+
+#ifdef MV_TRACE
+extern "C" MV_API void mv_trace_set_decode(void* buf) { mv::g_decode_trace = buf; }
+#endif

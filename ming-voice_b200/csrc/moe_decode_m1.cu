@@ -86,22 +86,36 @@ struct Stage {
   int du, dr, ne;      // down: first (expert, row) entry and the entry count
 };
 
-template <bool INT8>
+// Gate rows per stage: the largest power of two <= 8 with 2 RG rows (gate + up) in one stage.
+__host__ __device__ constexpr int rows_per_stage(int row_bytes) {
+  return 2 * 8 * row_bytes <= kStageBytes ? 8 : (2 * 4 * row_bytes <= kStageBytes ? 4 : (2 * 2 * row_bytes <= kStageBytes ? 2 : 1));
+}
+
+// Specialised for the hidden size H and the expert width I (the model's, so every offset, trip count and bound
+// below is a compile-time constant and the inner loops have no branches).
+template <bool INT8, int H, int I>
 __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) {
   using WT = W<INT8>;
   constexpr int VEC = WT::vec;
-  constexpr int kXJ = INT8 ? 1 : 2;  // 16-byte chunks per lane of a row's K quarter (H, I <= 2048)
+  constexpr int RG = rows_per_stage(H * WT::esz);
+  constexpr int DP0 = kStageBytes / (I * WT::esz);
+  constexpr int DP = DP0 < kNhMax ? DP0 : kNhMax;  // down rows per stage
+  constexpr int nvh = H / VEC, nqh = nvh / kGW;    // 16-byte chunks of a gate/up row; of its K quarter
+  constexpr int nvi = I / VEC, nqi = nvi / kGW;    // ... of a down row
+  constexpr int kXJ = (nqh > nqi ? nqh : nqi) > 32 ? 2 : 1;  // chunks per lane of a K quarter (at most 2)
+  static_assert(RG == 4 || RG == 8, "4 or 8 gate rows per stage");
+  static_assert(nvh % kGW == 0 && nvi % kGW == 0 && nqh <= 64 && nqi <= 64, "K quarters of at most 64 chunks");
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int grp = warp / kGW;  // group: owns ring slot grp
   const int kq = warp % kGW;   // K quarter of every row this warp takes
-  const int H = p.H, I = p.I;
   const int G = gridDim.x;
-  const int RG = p.RG, DP = p.DP, nhc = p.nh_cap;
+  const int nhc = p.nh_cap;
   const int n_static = p.n_static;
   const Layout Lo = layout(H, I, p.E, p.u_max, nhc, p.gsc_cap, RG, INT8);
+  (void)DP0;
   uint8_t* ring = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lo.bars);
   uint16_t* xn = reinterpret_cast<uint16_t*>(smem + Lo.xn);
@@ -271,26 +285,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
     named_bar(1, kThreads);
     if (tid == 0) MV_TRACE_AT(p, 1);
   }
-  // this lane's x values for its K quarter of the gate/up rows (chunks c = kq * nq + lane + 32 j)
-  const int nvh = H / VEC, nqh = (nvh + kGW - 1) / kGW, ceh = min(nvh, (kq + 1) * nqh);
+  // this lane's x values for its K quarter of the gate/up rows: chunks c = kq * nqh + lane + 32 j; a lane past the
+  // quarter's end reads the quarter's last chunk with x = 0 (so every lane runs the same branch-free code)
   float xv[kXJ][VEC];
 #pragma unroll
   for (int j = 0; j < kXJ; ++j) {
-    const int c = kq * nqh + lane + 32 * j;
-    const bool in = c < ceh;
+    const bool in = lane + 32 * j < nqh;
+    const int c = kq * nqh + (in ? lane + 32 * j : nqh - 1);
 #pragma unroll
     for (int e = 0; e < VEC; e += 8) {
-      const uint4 v = in ? *reinterpret_cast<const uint4*>(xn + c * VEC + e) : make_uint4(0, 0, 0, 0);
+      const uint4 v = *reinterpret_cast<const uint4*>(xn + c * VEC + e);
       const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int z = 0; z < 4; ++z) {
-        xv[j][e + 2 * z] = bf16lo(vv[z]);
-        xv[j][e + 2 * z + 1] = bf16hi(vv[z]);
+        xv[j][e + 2 * z] = in ? bf16lo(vv[z]) : 0.f;
+        xv[j][e + 2 * z + 1] = in ? bf16hi(vv[z]) : 0.f;
       }
     }
   }
+  int cofs[kXJ];  // byte offset of this lane's chunk j within a gate/up row
+#pragma unroll
+  for (int j = 0; j < kXJ; ++j) cofs[j] = (kq * nqh + (lane + 32 * j < nqh ? lane + 32 * j : nqh - 1)) * 16;
 
-  // ---- one gate/up stage: split K over the group's warps, SiLU(gate) * up * weight per row -> workspace
+  // ---- one gate/up stage: split K over the group's warps, SiLU(gate) * up * weight per row -> workspace. All 8
+  // rows of a batch are computed (rows past the stage's nr read stale slot data; their sums are never used).
   auto consume_gu = [&](const Stage& st) {
     const bool routed = st.walk == 1;
     const long long rw = static_cast<long long>(st.u - (routed ? n_static : 0)) * I + st.i;  // row in its walk
@@ -298,6 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
     const int sc0 = routed ? static_cast<int>(s_hi - s_lo + rw - r_lo) : static_cast<int>(rw - s_lo);
     float* gp = gpart + ((grp * 2 + (gcount & 1)) * 2 * RG) * kGW;
     if (ok) {
+#pragma unroll
       for (int h = 0; h < RG / 4; ++h) {  // batches of 4 gate rows + the 4 matching up rows
         float acc[8][2];
         float sc[8];
@@ -305,22 +324,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
         for (int r = 0; r < 8; ++r) {
           acc[r][0] = acc[r][1] = 0.f;
           sc[r] = 1.0f;
-          if (INT8 && h * 4 + (r & 3) < st.nr)
-            sc[r] = gsc[(r < 4 ? 0 : p.gsc_cap) + sc0 + h * 4 + (r & 3)];
+          if (INT8) sc[r] = gsc[(r < 4 ? 0 : p.gsc_cap) + sc0 + min(h * 4 + (r & 3), st.nr - 1)];
         }
 #pragma unroll
         for (int j = 0; j < kXJ; ++j) {
-          const int c = kq * nqh + lane + 32 * j;
-          if (c < ceh) {
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              if (h * 4 + (r & 3) < st.nr) {
-                const int row = (r < 4 ? 0 : RG) + h * 4 + (r & 3);
-                const uint4 wv = *reinterpret_cast<const uint4*>(slot + static_cast<size_t>(row) * row_b +
-                                                                 static_cast<size_t>(c) * 16);
-                chunk_fma<INT8>(acc[r][0], acc[r][1], wv, xv[j], sc[r]);
-              }
-            }
+          for (int r = 0; r < 8; ++r) {
+            const int row = (r < 4 ? 0 : RG) + h * 4 + (r & 3);
+            const uint4 wv = *reinterpret_cast<const uint4*>(slot + row * (H * WT::esz) + cofs[j]);
+            chunk_fma<INT8>(acc[r][0], acc[r][1], wv, xv[j], sc[r]);
           }
         }
         float v[8];
@@ -382,9 +394,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
   if (warp == 0) {
     for (int j = lane; j < p.E; j += 32) sel_r[j] = ld_cg_f32(p.logits_ws + j);
     __syncwarp();
+    if (tid == 0) MV_TRACE_AT(p, 14);
     const route::SelectCfg cfg{p.route_mode, p.E, p.top_k, p.n_group, p.topk_group, p.rscale, p.rbias};
     route::select_core(cfg, sel_r, sel_sc, pr_e, pr_w);
     __syncwarp();
+    if (tid == 0) MV_TRACE_AT(p, 15);
     if (blockIdx.x == 0) {  // router outputs: ids / weights with the static slots appended, logits
       const int NKT = p.top_k + n_static;
       for (int k = lane; k < NKT; k += 32) {
@@ -400,8 +414,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
       if (p.logits_out)
         for (int j = lane; j < p.E; j += 32) p.logits_out[j] = sel_r[j];
     }
+    if (tid == 0) MV_TRACE_AT(p, 16);
     table_warp<1>(pr_e, pr_w, p.top_k, p.top_k, p.E1, n_static, p.static_id, 1, e_id, e_ntok, e_tok, e_w, e_pbase,
                   misc, p.ws);
+    if (tid == 0) MV_TRACE_AT(p, 17);
   }
   named_bar(1, kThreads);
   if (tid == 0) MV_TRACE_AT(p, 4);
@@ -496,8 +512,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
   named_bar(1, kThreads);
   if (tid == 0) MV_TRACE_AT(p, 9);
 
-  // ---- down stages: split K, runs of up to 8 rows of one expert; the K quarters of each (expert, row) to ypart
-  const int nvi = I / VEC, nqi = (nvi + kGW - 1) / kGW, cei = min(nvi, (kq + 1) * nqi);
+  // ---- down stages: split K, runs of up to 8 rows of one expert; the K quarters of each (expert, row) to ypart.
+  // All 8 rows of a run are computed (rows past the run read other slot or shared data; never used).
+  int dofs[kXJ];  // byte offset of this lane's chunk j within a down row
+  bool din[kXJ];
+#pragma unroll
+  for (int j = 0; j < kXJ; ++j) {
+    din[j] = lane + 32 * j < nqi;
+    dofs[j] = (kq * nqi + (din[j] ? lane + 32 * j : nqi - 1)) * 16;
+  }
 #ifdef MV_TRACE
   int tk = 0;
 #endif
@@ -516,19 +539,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
       for (int k = 0; k < cur.ne;) {
         const int u = c.u, r0 = c.r;
         const int run = min(8, min(cur.ne - k, nh - r0));
-        if (u != au) {  // this lane's activation chunks of expert u
+        if (u != au) {  // this lane's activation chunks of expert u (0 past the quarter's end)
           const float* a_u = abuf + e_pbase[u] * I;
 #pragma unroll
           for (int j = 0; j < kXJ; ++j) {
-            const int ch = kq * nqi + lane + 32 * j;
 #pragma unroll
             for (int e = 0; e < VEC; e += 4) {
-              const float4 a4 = ch < cei ? *reinterpret_cast<const float4*>(a_u + ch * VEC + e)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-              av[j][e] = a4.x;
-              av[j][e + 1] = a4.y;
-              av[j][e + 2] = a4.z;
-              av[j][e + 3] = a4.w;
+              const float4 a4 = *reinterpret_cast<const float4*>(a_u + (dofs[j] / 16) * VEC + e);
+              av[j][e] = din[j] ? a4.x : 0.f;
+              av[j][e + 1] = din[j] ? a4.y : 0.f;
+              av[j][e + 2] = din[j] ? a4.z : 0.f;
+              av[j][e + 3] = din[j] ? a4.w : 0.f;
             }
           }
           au = u;
@@ -538,20 +559,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
           acc[r][0] = acc[r][1] = 0.f;
-          sc[r] = (INT8 && r < run) ? dsc[u * nhc + r0 + r] : 1.0f;
+          sc[r] = INT8 ? dsc[u * nhc + r0 + min(r, run - 1)] : 1.0f;
         }
+        const uint8_t* rows = slot + k * (I * WT::esz);
 #pragma unroll
         for (int j = 0; j < kXJ; ++j) {
-          const int ch = kq * nqi + lane + 32 * j;
-          if (ch < cei) {
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              if (r < run) {
-                const uint4 wv = *reinterpret_cast<const uint4*>(slot + static_cast<size_t>(k + r) * drow_b +
-                                                                 static_cast<size_t>(ch) * 16);
-                chunk_fma<INT8>(acc[r][0], acc[r][1], wv, av[j], sc[r]);
-              }
-            }
+          for (int r = 0; r < 8; ++r) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(rows + r * (I * WT::esz) + dofs[j]);
+            chunk_fma<INT8>(acc[r][0], acc[r][1], wv, av[j], sc[r]);
           }
         }
         float v[8];
@@ -597,25 +613,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
 int decode_m1_run(decode::Params& p, bool int8, cudaStream_t st) {
   using namespace decode;
   using namespace decode::m1;
-  const int H = p.H, I = p.I, esz = int8 ? 1 : 2, vec = int8 ? 16 : 8, kxj = int8 ? 1 : 2;
+  const int H = p.H, I = p.I, esz = int8 ? 1 : 2;
   if (p.M != 1 || !p.router) return kDecodeM1Unsuitable;
+  // the instantiated shapes: ming-voice's BASELINE block (H 2048, I 1408) and the released model's (1536, 512)
+  void (*kern)(Params) = nullptr;
+  if (H == 2048 && I == 1408)
+    kern = int8 ? decode_m1_kernel<true, 2048, 1408> : decode_m1_kernel<false, 2048, 1408>;
+  else if (H == 1536 && I == 512)
+    kern = int8 ? decode_m1_kernel<true, 1536, 512> : decode_m1_kernel<false, 1536, 512>;
+  if (kern == nullptr) return kDecodeM1Unsuitable;
   const int G = num_sms();
-  int RG = 1;  // gate rows per stage: the largest power of two <= 8 with 2 RG rows in a stage
-  while (RG * 2 <= 8 && 2 * (RG * 2) * H * esz <= kStageBytes) RG *= 2;
-  const int DP = static_cast<int>(kStageBytes / (static_cast<long long>(I) * esz));
-  const int nq_h = (H / vec + kGW - 1) / kGW, nq_i = (I / vec + kGW - 1) / kGW;
-  if ((RG != 4 && RG != 8) || DP < 1 || nq_h > 32 * kxj || nq_i > 32 * kxj || H % vec || I % vec ||
-      p.E > kWarps * G || p.top_k > 32)
-    return kDecodeM1Unsuitable;
+  if (p.E > kWarps * G || p.top_k > 32) return kDecodeM1Unsuitable;
+  const int RG = rows_per_stage(H * esz);
   p.RG = RG;
-  p.DP = DP < kNhMax ? DP : kNhMax;
   p.u_max = p.n_static + (p.top_k < p.E ? p.top_k : p.E);
   p.nh_cap = (H + G - 1) / G;
   if (p.nh_cap > kNhMax) return kDecodeM1Unsuitable;
   p.gsc_cap = int8 ? static_cast<int>((static_cast<long long>(p.u_max) * I + G - 1) / G + 4) : 0;
   const Layout L = layout(H, I, p.E, p.u_max, p.nh_cap, p.gsc_cap, RG, int8);
   if (L.total > 227u * 1024u) return kDecodeM1Unsuitable;
-  void (*kern)(Params) = int8 ? decode_m1_kernel<true> : decode_m1_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.total));
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(decode_m1)");
   cudaLaunchConfig_t cfg = {};
