@@ -319,6 +319,7 @@ def ep_prefill_lines(dev, world, rank, steps, warmup):
     ep = EPMoeBlock(blk, E, replicated=replicated)
     N = sum(O.PREFILL_LENS)
     x = O.make_tokens(N, seed=2 + rank).to(dev)
+    cap = ep.calibrate(x)  # the exchange capacity per peer, from this batch (before the timed region)
     for _ in range(warmup):
         ep.forward(x)
     torch.distributed.barrier()
@@ -332,11 +333,15 @@ def ep_prefill_lines(dev, world, rank, steps, warmup):
     t = torch.tensor([s_ev.elapsed_time(e_ev) / steps], dtype=torch.float64, device=dev)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     us = t.item() * 1e3
+    errs = ep.errors()
+    if errs:
+        raise RuntimeError(f"EP prefill device errors: {errs}")
     flops = O.prefill_flops(N) * world
     return {"tokens_per_gpu": N, "us_per_pass": round(us, 1), "tokens_per_s": round(world * N / us * 1e6, 0),
             "tflops": round(flops / us / 1e6, 1),
             "parallelism": f"ep{world}: experts 0-{EP_REPLICATED - 1} replicated, {E - EP_REPLICATED} round-robin",
-            "exchange": "NCCL all-to-all-v of token rows and weighted outputs", "flops_per_pass": flops}
+            "exchange": f"NCCL all-to-all of fixed capacity {cap} pairs per peer: bf16 rows out, fp32 outputs back "
+                        "(device-side plan / pack / combine, no host synchronisation)", "flops_per_pass": flops}
 
 
 def run_ours(args):

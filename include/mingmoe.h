@@ -190,6 +190,41 @@ MV_API int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_st
                           void* workspace, size_t workspace_bytes, void* stream);
 MV_API size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1, int w_dtype);
 
+/* mv_moe_prefill with fp32 outputs: out32 [N, H] f32 (contiguous) receives residual + sum_k wts * expert outputs,
+ * accumulated in fp32 and not rounded. For expert-parallel prefill, whose partial sums from several ranks are
+ * added before the one rounding to bf16 (ming-voice has no counterpart: it is single-GPU, engine.py:34). */
+MV_API int mv_moe_prefill_f32(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids,
+                              int ids_dtype, const float* wts, int N, int NK, const void* residual,
+                              long long residual_stride, float* out32, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* Expert-parallel prefill, the device side of one rank's dispatch and combine (ming-voice is single-GPU,
+ * engine.py:34, so these have no counterpart there; they implement the exchange of an expert-parallel block whose
+ * experts are placed by owner[E] (the rank holding routed expert e, or -1 when every rank holds it) and slot[E]
+ * (its index in the holding rank's stacks). Pair ids / weights are [N, NK] int32 / f32 with the K routed pairs
+ * first and the shared slots after them. Capacity `cap` pairs per peer; send_meta / recv_meta are
+ * [world][cap + 1][2] int32: (slot, weight bits) per place and the place count in entry cap. None of them
+ * synchronises the host.
+ *  mv_ep_plan     one CTA: ids_local / wts_local [N, NK] (local slot, or -1 for a pair held by another rank),
+ *                 pos [N, K] (d * cap + j for a pair sent to place j of peer d, else -1), send_src [world * cap]
+ *                 (source row of each place), send_meta. Places follow token order per peer. More than cap pairs
+ *                 for one peer: the excess pairs are dropped and workspace error 3 (capacity) is raised.
+ *                 workspace: mv_ep_workspace_bytes() bytes, header zeroed.
+ *  mv_ep_pack     send_rows [world * cap, H] bf16: row send_src of xn (row stride x_stride) for every place in use.
+ *  mv_ep_unpack   ids / wts [world * cap, NK] of the received rows: column 0 = (slot, weight) of a used place, the
+ *                 rest -1 / 0.
+ *  mv_ep_combine  out [N, H] bf16 = x + y_local + the returned fp32 outputs back[pos[n, k]] of n's remote pairs
+ *                 (k order), rounded once. */
+MV_API size_t mv_ep_workspace_bytes(void);
+MV_API int mv_ep_plan(const int* ids, const float* wts, int N, int NK, int K, const int* owner, const int* slot, int E,
+                      int rank, int world, int cap, int* ids_local, float* wts_local, int* pos, int* send_src,
+                      int* send_meta, void* workspace, size_t workspace_bytes, void* stream);
+MV_API int mv_ep_pack(const void* xn, long long x_stride, int H, const int* send_src, const int* send_meta, int world,
+                      int cap, void* send_rows, void* stream);
+MV_API int mv_ep_unpack(const int* recv_meta, int world, int cap, int NK, int* ids, float* wts, void* stream);
+MV_API int mv_ep_combine(const void* x, long long x_stride, const float* y_local, const float* back, const int* pos,
+                         int N, int K, int H, void* out, void* stream);
+
 /* Workspace for the fastest decode path (the tensor-core kernel, bf16 weights, H and I multiples of 128,
  * H <= 2048): larger than mv_moe_decode_workspace_bytes, which is the minimum (with the minimum the CUDA-core
  * kernel runs). Sized for M tokens with NK experts each from E1 stacked slots. */

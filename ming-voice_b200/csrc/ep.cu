@@ -1,0 +1,246 @@
+// Expert-parallel prefill: the device side of one rank's dispatch and combine (the exchange itself is two NCCL
+// all-to-alls of fixed size issued by the host; nothing here synchronises the host, so a whole step can be
+// captured in a CUDA graph).
+//
+// Placement (ming-voice is single-GPU, engine.py:34; expert parallelism is new): every rank holds the router,
+// the norm, the shared-expert slots and the replicated hot experts; each other ("cold") expert lives on one rank.
+// owner[e] = the rank holding routed expert e (-1: replicated, i.e. this rank), slot[e] = its index in the
+// holding rank's stacks.
+//
+//   mv_ep_plan      (one CTA) every routed pair of this rank's tokens, in token order: a pair whose expert lives
+//                   here keeps its local slot id; any other pair gets id -1 locally and a place j < cap in the
+//                   send block of its owner d (deterministic: pairs keep their token order per owner). Writes the
+//                   per-owner (slot, weight) metadata with the count in entry cap of each block, the source token
+//                   of each place, and pos[n, k] = d * cap + j (-1 for local pairs). More than cap pairs for one
+//                   owner: the excess pairs are dropped and the capacity error is raised in the workspace.
+//   mv_ep_pack      rows of the normalised tokens into the send blocks (one warp per place in use).
+//   mv_ep_unpack    received metadata -> ids / weights of the received rows (id -1 for unused places).
+//   mv_ep_combine   out[n] = bf16(x[n] + y_local[n] + sum over n's remote pairs, in k order, of their returned
+//                   fp32 outputs): one rounding, the same sum as one GPU computes.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace mv {
+namespace ep {
+
+constexpr int kMaxWorld = 8;
+constexpr int kPlanThreads = 1024;
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restrict__ ids, const float* __restrict__ wts,
+                                                            int N, int NK, int K, const int* __restrict__ owner,
+                                                            const int* __restrict__ slot, int E, int rank, int world,
+                                                            int cap, int* __restrict__ ids_local,
+                                                            float* __restrict__ wts_local, int* __restrict__ pos,
+                                                            int* __restrict__ send_src, int* __restrict__ send_meta,
+                                                            WsHeader* ws) {
+  __shared__ int s_warp[kPlanThreads / 32][kMaxWorld];
+  __shared__ int s_base[kMaxWorld];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const long long P = static_cast<long long>(N) * K;
+  const long long chunk = (P + kPlanThreads - 1) / kPlanThreads;
+  const long long p0 = chunk * t, p1 = min(P, p0 + chunk);
+  // pass 1: this thread's pairs per owner
+  int cnt[kMaxWorld];
+#pragma unroll
+  for (int d = 0; d < kMaxWorld; ++d) cnt[d] = 0;
+  for (long long q = p0; q < p1; ++q) {
+    const int n = static_cast<int>(q / K), k = static_cast<int>(q % K);
+    const int e = ids[static_cast<long long>(n) * NK + k];
+    const int d = (e >= 0 && e < E) ? owner[e] : -1;
+    if (d >= 0 && d != rank) {
+#pragma unroll
+      for (int dd = 0; dd < kMaxWorld; ++dd) cnt[dd] += dd == d ? 1 : 0;
+    }
+  }
+  // exclusive prefix over threads, per owner (warp shuffles, then the warp totals)
+  int pre[kMaxWorld];
+#pragma unroll
+  for (int d = 0; d < kMaxWorld; ++d) {
+    int v = cnt[d];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    pre[d] = v - cnt[d];
+    if (lane == 31) s_warp[warp][d] = v;
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int d = 0; d < kMaxWorld; ++d) {
+      const int tot = s_warp[lane][d];
+      int v = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      s_warp[lane][d] = v - tot;
+      if (lane == 31) s_base[d] = v;
+    }
+  }
+  __syncthreads();
+  int off[kMaxWorld];
+#pragma unroll
+  for (int d = 0; d < kMaxWorld; ++d) off[d] = s_warp[warp][d] + pre[d];
+  // pass 2: ids / weights of the local pass, places of the remote pairs
+  for (long long q = p0; q < p1; ++q) {
+    const int n = static_cast<int>(q / K), k = static_cast<int>(q % K);
+    const long long iq = static_cast<long long>(n) * NK + k;
+    const int e = ids[iq];
+    const int d = (e >= 0 && e < E) ? owner[e] : rank;
+    int pq = -1;
+    if (e >= 0 && e < E && d != rank && d >= 0) {
+      int j = 0;
+#pragma unroll
+      for (int dd = 0; dd < kMaxWorld; ++dd)
+        if (dd == d) j = off[dd]++;
+      if (j < cap) {
+        send_src[d * cap + j] = n;
+        send_meta[(static_cast<long long>(d) * (cap + 1) + j) * 2] = slot[e];
+        send_meta[(static_cast<long long>(d) * (cap + 1) + j) * 2 + 1] = __float_as_int(wts[iq]);
+        pq = d * cap + j;
+      } else {
+        raise_error(ws, kErrOverflow, static_cast<unsigned int>(d));
+      }
+      ids_local[iq] = -1;
+      wts_local[iq] = 0.f;
+    } else {
+      ids_local[iq] = (e >= 0 && e < E) ? slot[e] : -1;
+      wts_local[iq] = wts[iq];
+    }
+    pos[static_cast<long long>(n) * K + k] = pq;
+  }
+  // the shared-expert columns (k >= K) keep their (local) ids and weights
+  for (long long q = t; q < static_cast<long long>(N) * (NK - K); q += kPlanThreads) {
+    const long long iq = (q / (NK - K)) * NK + K + q % (NK - K);
+    ids_local[iq] = ids[iq];
+    wts_local[iq] = wts[iq];
+  }
+  if (t < world) send_meta[(static_cast<long long>(t) * (cap + 1) + cap) * 2] = min(s_base[t], cap);
+}
+
+// one warp per send place (d, j): row send_src[d, j] of xn -> send_rows[d * cap + j] (places past the count skip)
+__global__ void __launch_bounds__(256) pack_kernel(const uint16_t* __restrict__ xn, long long x_stride, int H,
+                                                   const int* __restrict__ send_src, const int* __restrict__ send_meta,
+                                                   int world, int cap, uint16_t* __restrict__ send_rows) {
+  const int lane = threadIdx.x & 31;
+  const long long total = static_cast<long long>(world) * cap;
+  for (long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < total;
+       w += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const int d = static_cast<int>(w / cap), j = static_cast<int>(w % cap);
+    if (j >= send_meta[(static_cast<long long>(d) * (cap + 1) + cap) * 2]) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(xn + static_cast<long long>(send_src[w]) * x_stride);
+    uint4* dst = reinterpret_cast<uint4*>(send_rows + w * H);
+    for (int v = lane; v < H / 8; v += 32) dst[v] = src[v];
+  }
+}
+
+// received places -> ids / weights of the received rows: column 0 the pair, the other columns -1
+__global__ void __launch_bounds__(256) unpack_kernel(const int* __restrict__ recv_meta, int world, int cap, int NK,
+                                                     int* __restrict__ ids, float* __restrict__ wts) {
+  const long long total = static_cast<long long>(world) * cap * NK;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / NK;
+    const int col = static_cast<int>(i % NK);
+    const int d = static_cast<int>(row / cap), j = static_cast<int>(row % cap);
+    const long long m = (static_cast<long long>(d) * (cap + 1) + j) * 2;
+    const bool valid = col == 0 && j < recv_meta[(static_cast<long long>(d) * (cap + 1) + cap) * 2];
+    ids[i] = valid ? recv_meta[m] : -1;
+    wts[i] = valid ? __int_as_float(recv_meta[m + 1]) : 0.f;
+  }
+}
+
+// out[n, 4c..4c+3] = bf16(x + y_local + the returned outputs of n's remote pairs in k order)
+__global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict__ x, long long x_stride,
+                                                      const float* __restrict__ y_local, const float* __restrict__ back,
+                                                      const int* __restrict__ pos, int N, int K, int H,
+                                                      uint16_t* __restrict__ out) {
+  const int h4 = H / 4;
+  const long long total = static_cast<long long>(N) * h4;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int n = static_cast<int>(i / h4), c = static_cast<int>(i % h4);
+    const uint2 xv = reinterpret_cast<const uint2*>(x + static_cast<long long>(n) * x_stride)[c];
+    const float4 yl = reinterpret_cast<const float4*>(y_local + static_cast<long long>(n) * H)[c];
+    float v0 = bf16lo(xv.x) + yl.x, v1 = bf16hi(xv.x) + yl.y, v2 = bf16lo(xv.y) + yl.z, v3 = bf16hi(xv.y) + yl.w;
+    for (int k = 0; k < K; ++k) {
+      const int pq = pos[static_cast<long long>(n) * K + k];
+      if (pq < 0) continue;
+      const float4 b = reinterpret_cast<const float4*>(back + static_cast<long long>(pq) * H)[c];
+      v0 += b.x;
+      v1 += b.y;
+      v2 += b.z;
+      v3 += b.w;
+    }
+    uint2 o;
+    o.x = static_cast<uint32_t>(f2bf(v0)) | (static_cast<uint32_t>(f2bf(v1)) << 16);
+    o.y = static_cast<uint32_t>(f2bf(v2)) | (static_cast<uint32_t>(f2bf(v3)) << 16);
+    reinterpret_cast<uint2*>(out + static_cast<long long>(n) * H)[c] = o;
+  }
+}
+
+}  // namespace ep
+}  // namespace mv
+
+using namespace mv;
+
+extern "C" size_t mv_ep_workspace_bytes(void) { return kWsHeaderBytes; }
+
+extern "C" int mv_ep_plan(const int* ids, const float* wts, int N, int NK, int K, const int* owner, const int* slot,
+                          int E, int rank, int world, int cap, int* ids_local, float* wts_local, int* pos,
+                          int* send_src, int* send_meta, void* workspace, size_t workspace_bytes, void* stream) {
+  if (ids == nullptr || wts == nullptr || owner == nullptr || slot == nullptr || ids_local == nullptr ||
+      wts_local == nullptr || pos == nullptr || send_src == nullptr || send_meta == nullptr)
+    return fail(MV_ERR_INVALID, "mv_ep_plan: null pointer argument");
+  if (world < 1 || world > ep::kMaxWorld || rank < 0 || rank >= world)
+    return fail(MV_ERR_INVALID, "mv_ep_plan: rank %d of world %d (at most %d ranks)", rank, world, ep::kMaxWorld);
+  if (N < 0 || K < 1 || NK < K || E < 1 || cap < 1) return fail(MV_ERR_INVALID, "mv_ep_plan: bad shape");
+  if (workspace == nullptr || workspace_bytes < kWsHeaderBytes)
+    return fail(MV_ERR_WORKSPACE, "mv_ep_plan: workspace of %zu bytes needed", kWsHeaderBytes);
+  ep::plan_kernel<<<1, ep::kPlanThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, wts, N, NK, K, owner, slot, E, rank, world, cap, ids_local, wts_local, pos, send_src, send_meta,
+      static_cast<WsHeader*>(workspace));
+  return cuda_status(cudaGetLastError(), "mv_ep_plan launch");
+}
+
+extern "C" int mv_ep_pack(const void* xn, long long x_stride, int H, const int* send_src, const int* send_meta,
+                          int world, int cap, void* send_rows, void* stream) {
+  if (xn == nullptr || send_src == nullptr || send_meta == nullptr || send_rows == nullptr)
+    return fail(MV_ERR_INVALID, "mv_ep_pack: null pointer argument");
+  if (H % 8 || x_stride % 8 || !aligned16(xn) || !aligned16(send_rows))
+    return fail(MV_ERR_ALIGN, "mv_ep_pack: 16-byte aligned rows needed");
+  const long long warps = static_cast<long long>(world) * cap;
+  const unsigned int blocks = static_cast<unsigned int>((warps + 7) / 8 < 148 * 8 ? (warps + 7) / 8 : 148 * 8);
+  ep::pack_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(xn), x_stride, H, send_src, send_meta, world, cap,
+      static_cast<uint16_t*>(send_rows));
+  return cuda_status(cudaGetLastError(), "mv_ep_pack launch");
+}
+
+extern "C" int mv_ep_unpack(const int* recv_meta, int world, int cap, int NK, int* ids, float* wts, void* stream) {
+  if (recv_meta == nullptr || ids == nullptr || wts == nullptr) return fail(MV_ERR_INVALID, "mv_ep_unpack: null");
+  const long long total = static_cast<long long>(world) * cap * NK;
+  const unsigned int blocks = static_cast<unsigned int>((total + 255) / 256 < 148 * 4 ? (total + 255) / 256 : 148 * 4);
+  ep::unpack_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(recv_meta, world, cap, NK,
+                                                                                              ids, wts);
+  return cuda_status(cudaGetLastError(), "mv_ep_unpack launch");
+}
+
+extern "C" int mv_ep_combine(const void* x, long long x_stride, const float* y_local, const float* back,
+                             const int* pos, int N, int K, int H, void* out, void* stream) {
+  if (x == nullptr || y_local == nullptr || back == nullptr || pos == nullptr || out == nullptr)
+    return fail(MV_ERR_INVALID, "mv_ep_combine: null pointer argument");
+  if (H % 4 || x_stride % 4 || !aligned16(y_local) || !aligned16(back))
+    return fail(MV_ERR_ALIGN, "mv_ep_combine: aligned rows needed");
+  if (N == 0) return MV_OK;
+  const long long total = static_cast<long long>(N) * H / 4;
+  const unsigned int blocks = static_cast<unsigned int>((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+  ep::combine_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), x_stride, y_local, back, pos, N, K, H, static_cast<uint16_t*>(out));
+  return cuda_status(cudaGetLastError(), "mv_ep_combine launch");
+}

@@ -661,11 +661,12 @@ extern "C" size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, in
   return layout(N, NK, H, I, E1, w_dtype == MV_I8).total;
 }
 
-extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids,
-                              int ids_dtype, const float* wts, int N, int NK, const void* residual,
-                              long long residual_stride, void* out, void* workspace, size_t workspace_bytes,
-                              void* stream) {
-  if (w == nullptr || (N > 0 && (x == nullptr || ids == nullptr || wts == nullptr || out == nullptr)))
+// The pipeline of mv_moe_prefill; with out32 != NULL the fp32 sums are accumulated straight into out32 [N, H]
+// (residual added in fp32 when given) and nothing is rounded to bf16.
+static int prefill_run(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids, int ids_dtype,
+                       const float* wts, int N, int NK, const void* residual, long long residual_stride, void* out,
+                       float* out32, void* workspace, size_t workspace_bytes, void* stream) {
+  if (w == nullptr || (N > 0 && (x == nullptr || ids == nullptr || wts == nullptr || (out == nullptr && out32 == nullptr))))
     return fail(MV_ERR_INVALID, "mv_moe_prefill: null pointer argument");
   if (ids_dtype != MV_I32 && ids_dtype != MV_I64) return fail(MV_ERR_INVALID, "mv_moe_prefill: ids must be i32 or i64");
   const bool int8 = w->w_dtype == MV_I8;
@@ -680,7 +681,8 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   if (static_cast<long long>(N) * NK > 0x7fffffffLL / 2) return fail(MV_ERR_INVALID, "mv_moe_prefill: too many pairs");
   if (N == 0) return MV_OK;
   const int esz = int8 ? 1 : 2;
-  if (!aligned16(w->w_gu) || !aligned16(w->w_d) || !aligned16(x) || !aligned16(out) ||
+  if (!aligned16(w->w_gu) || !aligned16(w->w_d) || !aligned16(x) || (out != nullptr && !aligned16(out)) ||
+      (out32 != nullptr && !aligned16(out32)) ||
       (residual != nullptr && (!aligned16(residual) || (residual_stride * 2) % 16)) || (x_stride * 2) % 16 ||
       (w->gu_sr * esz) % 16 || (w->gu_se * esz) % 16 || (w->d_sr * esz) % 16 || (w->d_se * esz) % 16)
     return fail(MV_ERR_ALIGN, "mv_moe_prefill: pointers and row strides must be 16-byte aligned");
@@ -697,7 +699,7 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
   int* bexp = reinterpret_cast<int*>(ws + L.off_bexp);
   uint16_t* xs = reinterpret_cast<uint16_t*>(ws + L.off_xs);
   uint16_t* abuf = reinterpret_cast<uint16_t*>(ws + L.off_a);
-  float* y32 = reinterpret_cast<float*>(ws + L.off_y32);
+  float* y32 = out32 != nullptr ? out32 : reinterpret_cast<float*>(ws + L.off_y32);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // int8: the GEMMs read bf16 copies of the experts in use (exact), contiguous in the workspace
   uint16_t* wgu16 = int8 ? reinterpret_cast<uint16_t*>(ws + L.off_wgu) : nullptr;
@@ -790,9 +792,28 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
     e = cudaLaunchKernelEx(&cfg, gemm_kernel, tm_xs, tm_wgu, tm_a, tm_wd, ga, g1, ready);
     if (e != cudaSuccess) return cuda_status(e, "grouped GEMM launch");
   }
+  if (out32 != nullptr) return MV_OK;
   const long long n4 = static_cast<long long>(N) * H / 4;
   long long blocks = (n4 + 255) / 256;
   if (blocks > G * 8) blocks = G * 8;
   finalize_kernel<<<static_cast<unsigned int>(blocks), 256, 0, st>>>(y32, n4, static_cast<uint16_t*>(out));
   return cuda_status(cudaGetLastError(), "finalize launch");
+}
+
+extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids,
+                              int ids_dtype, const float* wts, int N, int NK, const void* residual,
+                              long long residual_stride, void* out, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  if (out == nullptr && N > 0) return fail(MV_ERR_INVALID, "mv_moe_prefill: null pointer argument");
+  return prefill_run(w, x, x_stride, ids, ids_dtype, wts, N, NK, residual, residual_stride, out, nullptr, workspace,
+                     workspace_bytes, stream);
+}
+
+extern "C" int mv_moe_prefill_f32(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids,
+                                  int ids_dtype, const float* wts, int N, int NK, const void* residual,
+                                  long long residual_stride, float* out32, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  if (out32 == nullptr && N > 0) return fail(MV_ERR_INVALID, "mv_moe_prefill_f32: null pointer argument");
+  return prefill_run(w, x, x_stride, ids, ids_dtype, wts, N, NK, residual, residual_stride, nullptr, out32, workspace,
+                     workspace_bytes, stream);
 }

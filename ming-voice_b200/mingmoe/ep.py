@@ -6,19 +6,23 @@ other ("cold") experts: cold expert number c (in id order) lives on rank c % wor
 bias six experts take ~80 % of all routed pairs, so sharding them would serialise the step on their owners;
 replicating them costs 17 MB per expert of the 180 GB on each GPU.
 
-A prefill step on a rank's own packed tokens:
-  1. RMSNorm and routing locally (mv_rmsnorm, mv_route);
-  2. the pairs whose expert lives on another rank, sorted by owner rank (stable, so every rank sends in token
-     order): pair counts exchanged with one all-to-all, then the token rows (bf16 [H]) and their metadata
-     (slot of the expert on its owner, routing weight) with all-to-all-v -- the one exchange step of the block;
-  3. ONE tcgen05 grouped-GEMM pass (mv_moe_prefill) over the rank's own tokens and the received rows: an own
-     token carries the pairs whose expert this rank holds (the replicated hot experts, its share of the cold
-     ones, the shared expert; the other pairs -1, which the expert sort skips), a received row its one pair;
-  4. the received rows' weighted outputs travel back (all-to-all-v, the reverse split) and are added at the
-     origin in fp32 with the residual and the local output, rounded once.
-
-The exchange sizes are data dependent, so a step synchronises the host once (the split sizes); prefill is not
-graph-captured. No kernel reads another GPU's memory: everything remote arrives through NCCL.
+A prefill step on a rank's own packed tokens (CUDA path, no host synchronisation anywhere: the exchange has a
+fixed capacity `cap` of pairs per peer, so the step can be captured in a CUDA graph):
+  1. RMSNorm and routing locally (mv_rmsnorm, mv_route), the normalised rows written into the first N rows of one
+     [N + world * cap, H] buffer;
+  2. mv_ep_plan (one CTA) gives every pair whose expert lives here its local slot and every other pair a place in
+     its owner's send block (token order kept), mv_ep_pack copies those rows into the send blocks;
+  3. two NCCL all-to-alls of fixed size: the (slot, weight) metadata with each block's count, and the rows, which
+     land in the last world * cap rows of the buffer (the one exchange step of the block);
+  4. ONE tcgen05 grouped-GEMM pass (mv_moe_prefill_f32) over the own rows (local pairs; the rest -1, skipped by the
+     expert sort) and the received rows (their one pair; unused places -1), fp32 outputs;
+  5. the received rows' fp32 outputs go back with one more all-to-all and mv_ep_combine adds, per token, the
+     residual, the local sum and its remote pairs' outputs in pair order, rounding once to bf16 -- the same sum a
+     single GPU makes.
+More than `cap` pairs for one peer is an error recorded in the plan's workspace (the excess pairs are dropped);
+`plan_capacity` measures what a batch needs. No kernel reads another GPU's memory: everything remote arrives
+through NCCL. With an `experts_fn` (the CPU tests) the same step runs on torch tensors with data-dependent
+all-to-all sizes instead.
 """
 from __future__ import annotations
 
@@ -53,7 +57,7 @@ class EPMoeBlock:
     `experts_fn(x, ids, wts)` computes weight * expert(x) per row on this rank's stacks (defaults to the CUDA
     grouped GEMM; the CPU tests pass a reference)."""
 
-    def __init__(self, block, E: int, group=None, replicated=(), experts_fn=None):
+    def __init__(self, block, E: int, group=None, replicated=(), experts_fn=None, cap=None):
         self.block = block
         self.group = group
         self.world = dist.get_world_size(group)
@@ -64,8 +68,12 @@ class EPMoeBlock:
         own = torch.tensor(owner, dtype=torch.long)
         self.owner = torch.where(own < 0, torch.full_like(own, self.rank), own)
         self.slot = torch.tensor(slot, dtype=torch.long)
+        self._owner_raw = torch.tensor(owner, dtype=torch.int32)  # -1 = replicated (held here)
         self.n_shared = len(block.shared_ids)
+        self.cuda_path = experts_fn is None
         self.experts_fn = experts_fn or self._experts_cuda
+        self.cap = cap
+        self._bufs = {}
 
     # ------------------------------------------------------------------------------------------ pieces
     def _experts_cuda(self, x, ids, wts, residual=None):
@@ -83,9 +91,112 @@ class EPMoeBlock:
     def _a2a(self, out, inp, out_splits, in_splits):
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
+    # ------------------------------------------------------------------------------------------ forward (CUDA)
+    def calibrate(self, x, headroom=1.25):
+        """Set the per-peer capacity from a representative batch: the largest count of pairs any rank sends to one
+        peer (plan_capacity, one host synchronisation), with headroom, rounded up to 16."""
+        need = self.plan_capacity(x)
+        self.cap = max(16, (int(need * headroom) + 15) // 16 * 16)
+        return self.cap
+
+    def plan_capacity(self, x):
+        """The largest number of pairs this rank's tokens x send to one peer, over all ranks (one host
+        synchronisation and one all-reduce: for sizing `cap` outside the timed or captured path)."""
+        b = self.block
+        import fused_ops
+        xn = fused_ops.rms_norm(x, b.norm_w, b.eps) if b.norm_w is not None else x
+        ids, _, _ = b.route(xn)
+        own = self.owner.to(x.device)[ids[:, :b.top_k].long()]
+        cnt = torch.stack([(own == d).sum() for d in range(self.world) if d != self.rank] or
+                          [torch.zeros((), dtype=torch.long, device=x.device)]).max().reshape(1)
+        dist.all_reduce(cnt, op=dist.ReduceOp.MAX, group=self.group)
+        return int(cnt.item())
+
+    def _buffers(self, N, cap, dev):
+        key = (N, cap, dev)
+        bf = self._bufs.get(key)
+        if bf is None:
+            b, W = self.block, self.world
+            R, NK, H = W * cap, b.nk, b.H
+            bf = dict(
+                xall=torch.empty(N + R, H, dtype=torch.bfloat16, device=dev),
+                ids=torch.empty(N, NK, dtype=torch.int32, device=dev),
+                wts=torch.empty(N, NK, dtype=torch.float32, device=dev),
+                logits=torch.empty(N, b.E, dtype=torch.float32, device=dev),
+                ids_all=torch.empty(N + R, NK, dtype=torch.int32, device=dev),
+                wts_all=torch.empty(N + R, NK, dtype=torch.float32, device=dev),
+                pos=torch.empty(N, b.top_k, dtype=torch.int32, device=dev),
+                send_src=torch.zeros(R, dtype=torch.int32, device=dev),
+                send_meta=torch.zeros(W, cap + 1, 2, dtype=torch.int32, device=dev),
+                recv_meta=torch.zeros(W, cap + 1, 2, dtype=torch.int32, device=dev),
+                send_rows=torch.zeros(R, H, dtype=torch.bfloat16, device=dev),
+                y32=torch.empty(N + R, H, dtype=torch.float32, device=dev),
+                back=torch.empty(R, H, dtype=torch.float32, device=dev),
+                out=torch.empty(N, H, dtype=torch.bfloat16, device=dev),
+                owner=self._owner_raw.to(dev),
+                slot=self.slot.to(torch.int32).to(dev),
+            )
+            self._bufs[key] = bf
+        return bf
+
+    def _forward_cuda(self, x):
+        import ctypes as C
+        import fused_ops
+        from . import _lib as L
+        b = self.block
+        N, H = x.shape
+        if x.dtype != torch.bfloat16 or x.stride(1) != 1:
+            raise TypeError("EP prefill: x must be bf16 with a unit inner stride")
+        dev = x.device
+        cap = self.cap if self.cap is not None else self.calibrate(x)  # (first call without a capacity: measured)
+        W, K, NK = self.world, b.top_k, b.nk
+        R = W * cap
+        bf = self._buffers(N, cap, dev)
+        st = L.stream_ptr(dev)
+        lib = L.lib()
+        xall = bf["xall"]
+        xn = xall[:N]
+        if b.norm_w is not None:
+            L.check(lib.mv_rmsnorm(L.ptr(x), L.MV_BF16, x.stride(0), L.ptr(b.norm_w), L.MV_BF16, L.ptr(xn), L.MV_BF16,
+                                   N, H, C.c_float(b.eps), st), "mv_rmsnorm")
+        else:
+            xn.copy_(x)
+        fused_ops.moe_route(xn, b.router_w, b.router_bias, b.n_group, b.topk_group, K, b.route_scale, bf["logits"],
+                            bf["ids"], bf["wts"], mode=b.route_mode, n_shared=len(b.shared_ids),
+                            shared_id=b.shared_ids[0] if b.shared_ids else b.E, w_scale=b.router_s)
+        ws = L.workspace("ep", int(lib.mv_ep_workspace_bytes()), dev)
+        L.check(lib.mv_ep_plan(L.ptr(bf["ids"]), L.ptr(bf["wts"]), N, NK, K, L.ptr(bf["owner"]), L.ptr(bf["slot"]),
+                               self.E, self.rank, W, cap, L.ptr(bf["ids_all"]), L.ptr(bf["wts_all"]), L.ptr(bf["pos"]),
+                               L.ptr(bf["send_src"]), L.ptr(bf["send_meta"]), L.ptr(ws), ws.numel(), st), "mv_ep_plan")
+        L.check(lib.mv_ep_pack(L.ptr(xn), xn.stride(0), H, L.ptr(bf["send_src"]), L.ptr(bf["send_meta"]), W, cap,
+                               L.ptr(bf["send_rows"]), st), "mv_ep_pack")
+        dist.all_to_all_single(bf["recv_meta"], bf["send_meta"], group=self.group)
+        dist.all_to_all_single(xall[N:], bf["send_rows"], group=self.group)
+        L.check(lib.mv_ep_unpack(L.ptr(bf["recv_meta"]), W, cap, NK, L.ptr(bf["ids_all"][N:]),
+                                 L.ptr(bf["wts_all"][N:]), st), "mv_ep_unpack")
+        wst = moe.weights_struct(b.w_gu, b.w_d, b.s_gu, b.s_d)
+        nbytes = lib.mv_moe_prefill_workspace_bytes(N + R, NK, H, b.I, b.w_gu.shape[0], L.dt(b.w_gu))
+        pws = L.workspace("prefill", nbytes, dev)
+        L.check(lib.mv_moe_prefill_f32(C.byref(wst), L.ptr(xall), H, L.ptr(bf["ids_all"]), L.MV_I32,
+                                       L.ptr(bf["wts_all"]), N + R, NK, None, 0, L.ptr(bf["y32"]), L.ptr(pws),
+                                       pws.numel(), st), "mv_moe_prefill_f32")
+        dist.all_to_all_single(bf["back"], bf["y32"][N:], group=self.group)
+        out = bf["out"]
+        L.check(lib.mv_ep_combine(L.ptr(x), x.stride(0), L.ptr(bf["y32"]), L.ptr(bf["back"]), L.ptr(bf["pos"]), N, K,
+                                  H, L.ptr(out), st), "mv_ep_combine")
+        return out
+
+    def errors(self):
+        """Device-side errors of the plan (capacity exceeded: code 3, info = the peer); host-synchronising."""
+        from . import _lib as L
+        errs = L.all_workspace_errors(clear=True)
+        return {k: v for k, v in errs.items() if k[0] == "ep"}
+
     # ------------------------------------------------------------------------------------------ forward
     def forward(self, x):
         """h + MoE(rms_norm(h)) for this rank's N packed tokens x [N, H] bf16."""
+        if self.cuda_path and x.is_cuda:
+            return self._forward_cuda(x)
         b = self.block
         N, H = x.shape
         K, dev = b.top_k, x.device

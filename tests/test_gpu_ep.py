@@ -1,5 +1,7 @@
-"""Expert-parallel prefill on 2 GPUs over NCCL (skipped with fewer than 2 GPUs): each rank's output equals
-the single-GPU block on its own tokens (both through the CUDA kernels)."""
+"""Expert-parallel prefill on 2 GPUs over NCCL (skipped with fewer than 2 GPUs): the device-planned step (plan,
+pack, fixed-capacity all-to-alls, one grouped-GEMM pass, combine) gives each rank the block's output on its own
+tokens within the BASELINE tolerance of the fp32 oracle (max-abs 2e-2, mean-rel = sum|d| / sum|ref| 1e-2), and
+a capacity below the batch's need is reported as device error 3."""
 import os
 import socket
 
@@ -31,10 +33,20 @@ def _worker(rank, world, port, q):
         blk = MoeBlock.from_params(loc, router_bias=bias)
         ep = EPMoeBlock(blk, 16, replicated=(0, 1))
         x = O.make_tokens(300 + 37 * rank, H=1024, seed=rank)
-        y = ep.forward(x.cuda())
         ref, _, _, _ = O.moe_block(x, p, top_k=6, bias=bias)
+        xc = x.cuda()
+        cap = ep.calibrate(xc)  # capacity from this batch (one host synchronisation)
+        for _ in range(2):  # the device-planned step, twice on the same buffers
+            y = ep.forward(xc).clone()
+        torch.cuda.synchronize()
+        errs = ep.errors()
         d = (y.float().cpu() - ref).abs()
-        q.put((rank, d.max().item(), (d.sum() / ref.abs().sum()).item()))
+        # a capacity below what the batch needs: the excess pairs are dropped and the plan reports it
+        ep_small = EPMoeBlock(blk, 16, replicated=(0, 1), cap=max(1, cap // 4))
+        ep_small.forward(xc)
+        torch.cuda.synchronize()
+        small_errs = ep_small.errors()
+        q.put((rank, d.max().item(), (d.sum() / ref.abs().sum()).item(), errs, sorted(c for c, _ in small_errs.values())))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -57,5 +69,7 @@ def test_ep_prefill_two_gpus():
             pr.kill()
     assert all(pr.exitcode == 0 for pr in procs)
     for _ in range(2):
-        rank, mx, mr = q.get(timeout=5)
+        rank, mx, mr, errs, small = q.get(timeout=5)
         assert mx <= MAX_ABS and mr <= MEAN_REL, (rank, mx, mr)
+        assert not errs, errs
+        assert small == [3], small  # capacity exceeded (code 3)
