@@ -12,11 +12,15 @@ whole-job time per block-token (lower is better; N > 1 runs independent replicas
 
 Keys beyond the base contract: roofline (HBM, measured copy peak), cpu_baseline (the oracle's torch-eager
 fp32 block on the host cores), e2e (the same metric through the public MoeBlock.decode API with the token
-copied host->device and the result device->host every step), gpu_launches, clocks; prefill (BASELINE
-the 2043-token ragged pass in a CUDA graph on one GPU, expert parallel over N > 1 ranks) with its
-tensor roofline; int8_decode (BASELINE configs[2] at M=1 through the same 16-layer graph chain, one GPU) with
-its HBM roofline. --decode-m M measures the other configs[1] token counts, --prefill-only the prefill pass
-alone, --no-prefill / --no-int8 skip those parts.
+copied host->device and the result device->host every step), gpu_launches, clocks (sampled from the first timed
+region to the end of the last); decode_sweep (M = 1, 2, 4, 8, 16 through the same graph
+chain, us/token and HBM fraction); int8_decode (configs[2] at M = 1, 4, 16, with its HBM roofline); prefill
+(configs[3]: the 2043-token ragged pass in a CUDA graph on one GPU, expert parallel over N > 1 ranks, weak
+scaling) with its tensor roofline; stack_prefill (configs[4](b): 8192 tokens through the 16 layers, strong
+scaling over N ranks); reference_kernels (why the reference's Triton kernels are not timed here). --decode-m M
+measures the headline at another token count, --prefill-only the prefill pass alone; --no-prefill / --no-int8 /
+--no-sweep / --no-stack skip those parts. --impl reference times the reference's CPU path (the oracle's fp32
+restatement) on the same 16-layer decode workload.
 """
 from __future__ import annotations
 
@@ -142,11 +146,11 @@ def make_stack(device, layers, seed=3, int8=False):
     return blocks
 
 
-def int8_decode_lines(dev, steps, warmup, layers=16, Md=1):
-    """BASELINE configs[2] (int8 weights, bf16 scales) at decode M=1, through the same 16-layer graph chain as the
-    headline: us per block-token and its HBM roofline (int8 bytes + bf16 scales)."""
+def chain_us_per_block(blocks, dev, Md, steps, warmup, ids=None):
+    """Device time per block of an Md-token step through the stack, one CUDA graph per step (Md tokens, seeded),
+    and the number of distinct routed experts of the first block's step."""
     from oracle import moe_oracle as O
-    blocks = make_stack(dev, layers, seed=4, int8=True)
+    layers = len(blocks)
     bufs = [torch.empty(Md, H, dtype=torch.bfloat16, device=dev) for _ in range(layers + 1)]
     bufs[0].copy_(O.make_tokens(Md, seed=3).to(dev))
     ids = torch.empty(Md, TOPK + 2, dtype=torch.int32, device=dev)
@@ -177,15 +181,45 @@ def int8_decode_lines(dev, steps, warmup, layers=16, Md=1):
     torch.cuda.synchronize()
     us = s_ev.elapsed_time(e_ev) / steps * 1e3 / layers
     U = O.distinct_experts(ids.cpu()[:, :TOPK])
-    byts = O.decode_bytes(U, M=Md, esz=1, scale_bytes=2)
+    del graph
+    return us, U
+
+
+def decode_sweep_lines(blocks, dev, steps, warmup, ms=(1, 2, 4, 8, 16)):
+    """decode at M in {1, 2, 4, 8, 16} tokens through the same 16-layer graph chain: us per
+    token and the HBM roofline of the weights touched (U distinct routed experts + the shared expert + router)."""
+    from oracle import moe_oracle as O
     peak, _ = peaks()
-    achieved = byts / (us * 1e-6) / 1e9
-    del graph, blocks
+    out = []
+    for Md in ms:
+        us, U = chain_us_per_block(blocks, dev, Md, steps, warmup)
+        byts = O.decode_bytes(U, M=Md)
+        gbs = byts / (us * 1e-6) / 1e9
+        out.append({"M": Md, "us_per_token": round(us / Md, 3), "us_per_block": round(us, 2), "routed_experts_hit": U,
+                    "bytes_per_block": byts, "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4)})
+    return out
+
+
+def int8_decode_lines(dev, steps, warmup, layers=16, ms=(1, 4, 16)):
+    """BASELINE configs[2] (int8 weights, bf16 scales) at decode M in {1, 4, 16}, through the same 16-layer graph chain
+    as the headline: us per token and the HBM roofline (int8 bytes + bf16 scales)."""
+    from oracle import moe_oracle as O
+    blocks = make_stack(dev, layers, seed=4, int8=True)
+    peak, _ = peaks()
+    rows = []
+    for Md in ms:
+        us, U = chain_us_per_block(blocks, dev, Md, steps, warmup)
+        byts = O.decode_bytes(U, M=Md, esz=1, scale_bytes=2)
+        achieved = byts / (us * 1e-6) / 1e9
+        rows.append({"M": Md, "us_per_token": round(us / Md, 3), "us_per_block": round(us, 2),
+                     "routed_experts_hit": U, "bytes_per_block": byts,
+                     "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                                  "frac": round(achieved / peak, 4)}})
+    del blocks
     torch.cuda.empty_cache()
-    return {"metric": "int8 decode us/token (BASELINE configs[2], M=1, 16-layer graph chain)",
-            "value": round(us / Md, 3), "unit": "us/token", "bytes_per_block": byts,
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4)}}
+    m1 = rows[0]
+    return {"metric": "int8 decode us/token (BASELINE configs[2], 16-layer graph chain)", "value": m1["us_per_token"],
+            "unit": "us/token", "bytes_per_block": m1["bytes_per_block"], "roofline": m1["roofline"], "sweep": rows}
 
 
 def cpu_block_time_us(reps=5):
@@ -218,27 +252,38 @@ def run_reference(args):
     rank, world, _ = dist_setup(args.gpus) if int(os.environ.get("WORLD_SIZE", "1")) > 1 else (0, 1, 0)
     if rank != 0:
         return
-    # the reference's CPU torch-eager path (restated in oracle/), all host threads, a bounded sample per step
+    # the reference's CPU torch-eager path (restated in oracle/), all host threads: the headline workload, one token
+    # through a 16-layer chain of fp32 blocks per step (the blocks share one set of weights: CPU time does not
+    # depend on their values, and 16 distinct fp32 blocks would hold 37 GB of host memory)
     from oracle import moe_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
     p = O.make_block_params(seed=3, dtype=torch.float32)
-    x = O.make_tokens(1, seed=3, dtype=torch.float32)
+    x0 = O.make_tokens(1, seed=3, dtype=torch.float32)
+
+    def step():
+        h = x0
+        for _ in range(args.layers):
+            h = O.moe_block(h, p)[0]
+        return h
+
     for _ in range(args.warmup):
-        O.moe_block(x, p)
+        step()
     ts = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.moe_block(x, p)
-        ts.append((time.perf_counter() - t0) * 1e6)
+        step()
+        ts.append((time.perf_counter() - t0) * 1e6 / args.layers)
     v = sum(ts) / len(ts)
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 2), "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v / 1e3, 4), "higher_is_better": False,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "decode M=1, one MoE block (CPU torch-eager reference path, fp32)",
-                   "H": H, "I": I, "E": E, "top_k": TOPK, "shared_I": IS},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v * args.layers / 1e3, 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decode M=1 through a {args.layers}-layer chain of MoE blocks (BASELINE configs[1] "
+                               "at M=1, run as configs[4](a)); CPU torch-eager reference path, fp32",
+                   "tokens_per_step": 1, "layers": args.layers, "H": H, "I": I, "E": E, "top_k": TOPK,
+                   "shared_I": IS},
         "cpu_baseline": {"value": round(v, 2), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": "1 token through 1 block per step (the 16-layer step scaled per block)"},
+                         "sample": f"1 token through {args.layers} fp32 blocks per step, us per block-token"},
         "e2e": {"value": round(v, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -344,6 +389,81 @@ def ep_prefill_lines(dev, world, rank, steps, warmup):
                         "(device-side plan / pack / combine, no host synchronisation)", "flops_per_pass": flops}
 
 
+def stack_prefill_lines(dev, world, rank, steps, warmup, blocks=None, layers=LAYERS, tokens=8192):
+    """BASELINE configs[4](b): 8 packed sequences of 1024 tokens (8192) through the 16-layer stack, one step = the
+    whole prefill. One GPU: MoeBlock.prefill per layer (norm, router, expert sort, grouped GEMMs, finalize) on the
+    decode stack's blocks. N ranks: expert parallel, strong scaling (8192 / N tokens per rank; every rank holds
+    the router, norm, shared expert and experts 0-7 of each layer and its round-robin share of the others)."""
+    from oracle import moe_oracle as O
+    per_rank = tokens // world
+    x = O.make_tokens(per_rank, seed=30 + rank).to(dev)
+    if world == 1:
+        fwd_blocks = blocks
+
+        def step():
+            h = x
+            for blk in fwd_blocks:
+                h = blk.prefill(h)
+            return h
+    else:
+        from mingmoe.block import MoeBlock
+        from mingmoe.ep import EPMoeBlock, placement
+        replicated = tuple(range(EP_REPLICATED))
+        stacks = placement(E, world, replicated)[2]
+        n_loc = len(stacks[rank])
+        E1 = E + IS // I
+        sel = torch.tensor(stacks[rank] + list(range(E, E1)), device=dev)
+        g = torch.Generator(device=dev).manual_seed(3)  # the same weights on every rank
+        eps_blocks = []
+        for _ in range(layers):
+            w_gu = (torch.randn(E1, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            w_d = (torch.randn(E1, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            rw = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            blk = MoeBlock(w_gu.index_select(0, sel).contiguous(), w_d.index_select(0, sel).contiguous(), rw,
+                           torch.ones(H, dtype=torch.bfloat16, device=dev), top_k=TOPK,
+                           shared_ids=tuple(range(n_loc, n_loc + E1 - E)), eps=1e-6)
+            del w_gu, w_d
+            eps_blocks.append(EPMoeBlock(blk, E, replicated=replicated))
+        h = x
+        for ep in eps_blocks:  # the exchange capacity of each layer, from this batch (before the timed region)
+            ep.calibrate(h)
+            h = ep.forward(h).clone()
+
+        def step():
+            h = x
+            for ep in eps_blocks:
+                h = ep.forward(h)
+            return h
+    for _ in range(warmup):
+        step()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
+    s_ev.record()
+    for _ in range(steps):
+        step()
+    e_ev.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s_ev.elapsed_time(e_ev) / steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        errs = {k: v for ep in eps_blocks for k, v in ep.errors().items()}
+        if errs:
+            raise RuntimeError(f"stack prefill EP device errors: {errs}")
+    ms = t.item()
+    flops = O.prefill_flops(per_rank * world) * layers
+    tf_peak, tf_kind = peaks_tensor()
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {"metric": f"prefill tokens/s (BASELINE configs[4](b): {tokens} tokens through {layers} layers, "
+                      + ("1 GPU" if world == 1 else f"expert parallel over {world} GPUs, strong scaling") + ")",
+            "tokens": per_rank * world, "tokens_per_gpu": per_rank, "layers": layers, "ms_per_step": round(ms, 3),
+            "tokens_per_s": round(per_rank * world / (ms * 1e-3), 0), "tflops": round(tflops, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tf_peak * world, "unit": "TFLOP/s",
+                         "frac": round(tflops / (tf_peak * world), 4),
+                         "note": f"algorithmic FLOPs / step time; peak {tf_kind}" + (f" x {world} GPUs" if world > 1 else "")}}
+
+
 def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -382,15 +502,16 @@ def run_ours(args):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    with ClockSampler(local) as clk:
-        barrier()
-        s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
-        s_ev.record()
-        for _ in range(args.steps):
-            graph.replay()
-        e_ev.record()
-        barrier()
-        elapsed_ms = s_ev.elapsed_time(e_ev)
+    # clocks are sampled from the first timed region to the end of the last (decode, e2e, prefill, int8, sweep, stack)
+    clk = ClockSampler(local).__enter__()
+    barrier()
+    s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
+    s_ev.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e_ev.record()
+    barrier()
+    elapsed_ms = s_ev.elapsed_time(e_ev)
     t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -429,6 +550,14 @@ def run_ours(args):
     q8 = None
     if world == 1 and not args.no_int8 and Md == 1:
         q8 = int8_decode_lines(dev, max(3, min(args.steps, 300)), args.warmup, layers=LAYERS)
+    sweep = None
+    if world == 1 and not args.no_sweep and Md == 1:
+        sweep = decode_sweep_lines(blocks, dev, max(3, min(args.steps, 100)), args.warmup, ms=(2, 4, 8, 16))
+    stack = None
+    if not args.no_stack:
+        stack = stack_prefill_lines(dev, world, rank, max(3, min(args.steps, 10)), args.warmup, blocks=blocks,
+                                    layers=LAYERS)
+    clk.__exit__()
     peak, peak_kind = peaks()
     byts = O.decode_bytes(U, M=Md)  # algorithmic bytes of one block step
     achieved = byts / (us_per_block * 1e-6) / 1e9
@@ -468,6 +597,19 @@ def run_ours(args):
                                                    + (f" x {world} GPUs" if world > 1 else "")}}
         if q8 is not None:
             out["int8_decode"] = q8
+        if sweep is not None:
+            m1 = {"M": 1, "us_per_token": out["value"], "us_per_block": round(us_per_block, 2),
+                  "routed_experts_hit": U, "bytes_per_block": byts, "hbm_gbs": round(achieved, 1),
+                  "hbm_frac": round(achieved / peak, 4)}
+            out["decode_sweep"] = {"metric": "decode us/token at M tokens (BASELINE configs[1], 16-layer graph chain)",
+                                   "rows": [m1] + sweep}
+        if stack is not None:
+            out["stack_prefill"] = stack
+        out["reference_kernels"] = {
+            "unavailable": "the reference's own GPU kernels are Triton source inside the ming-voice application, "
+                           "which is not an installable package (no setup.py / pyproject.toml), so they cannot be "
+                           "installed into baseline/_ref or travel to the GPU box; their numerics are pinned on the "
+                           "CPU by the golden fixtures (tests/golden) instead"}
     if world > 1:
         torch.distributed.barrier()
         del graph
@@ -485,6 +627,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="blocks in the chain (1 = the small profiling case)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) measurement")
     ap.add_argument("--no-int8", action="store_true", help="skip the int8 decode (configs[2]) measurement")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the decode token-count sweep (configs[1])")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 16-layer 8192-token prefill (configs[4](b))")
     ap.add_argument("--decode-m", type=int, default=1, choices=range(1, 17), metavar="M",
                     help="tokens per decode step (1 = the headline; 2..16 = the other configs[1] points)")
     ap.add_argument("--prefill-only", action="store_true",

@@ -192,11 +192,14 @@ MV_API size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, int E1
 
 /* mv_moe_prefill with fp32 outputs: out32 [N, H] f32 (contiguous) receives residual + sum_k wts * expert outputs,
  * accumulated in fp32 and not rounded. For expert-parallel prefill, whose partial sums from several ranks are
- * added before the one rounding to bf16 (ming-voice has no counterpart: it is single-GPU, engine.py:34). */
-MV_API int mv_moe_prefill_f32(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids,
-                              int ids_dtype, const float* wts, int N, int NK, const void* residual,
-                              long long residual_stride, float* out32, void* workspace, size_t workspace_bytes,
-                              void* stream);
+ * added before the one rounding to bf16 (ming-voice has no counterpart: it is single-GPU, engine.py:34). Rows
+ * [0, n_x) are read from x (row stride x_stride), rows [n_x, N) from x2 (row stride x2_stride; NULL when
+ * n_x == N): a rank's own rows and the rows it received, each where it lies. max_ctas > 0 limits the persistent
+ * GEMM to that many SMs; 0 = all SMs. */
+MV_API int mv_moe_prefill_f32(const mv_moe_weights* w, const void* x, long long x_stride, int n_x, const void* x2,
+                              long long x2_stride, const void* ids, int ids_dtype, const float* wts, int N, int NK,
+                              const void* residual, long long residual_stride, float* out32, int max_ctas,
+                              void* workspace, size_t workspace_bytes, void* stream);
 
 /* Expert-parallel prefill, the device side of one rank's dispatch and combine (ming-voice is single-GPU,
  * engine.py:34, so these have no counterpart there; they implement the exchange of an expert-parallel block whose
@@ -210,9 +213,11 @@ MV_API int mv_moe_prefill_f32(const mv_moe_weights* w, const void* x, long long 
  *                 (source row of each place), send_meta. Places follow token order per peer. More than cap pairs
  *                 for one peer: the excess pairs are dropped and workspace error 3 (capacity) is raised.
  *                 workspace: mv_ep_workspace_bytes() bytes, header zeroed.
- *  mv_ep_pack     send_rows [world * cap, H] bf16: row send_src of xn (row stride x_stride) for every place in use.
- *  mv_ep_unpack   ids / wts [world * cap, NK] of the received rows: column 0 = (slot, weight) of a used place, the
- *                 rest -1 / 0.
+ *  mv_ep_pack     send_rows [world * cap, H + 8] bf16 wire rows: row send_src of xn (row stride x_stride) and a
+ *                 16-byte tail (slot, weight bits, in-use flag 1, 0) for every place in use; the other places get a
+ *                 zero tail only. Rows and metadata then cross in one all-to-all.
+ *  mv_ep_unpack   ids / wts [world * cap, NK] of the received wire rows recv_rows [world * cap, H + 8]: column 0 =
+ *                 (slot, weight) of a place in use, the rest -1 / 0.
  *  mv_ep_combine  out [N, H] bf16 = x + y_local + the returned fp32 outputs back[pos[n, k]] of n's remote pairs
  *                 (k order), rounded once. */
 MV_API size_t mv_ep_workspace_bytes(void);
@@ -221,7 +226,7 @@ MV_API int mv_ep_plan(const int* ids, const float* wts, int N, int NK, int K, co
                       int* send_meta, void* workspace, size_t workspace_bytes, void* stream);
 MV_API int mv_ep_pack(const void* xn, long long x_stride, int H, const int* send_src, const int* send_meta, int world,
                       int cap, void* send_rows, void* stream);
-MV_API int mv_ep_unpack(const int* recv_meta, int world, int cap, int NK, int* ids, float* wts, void* stream);
+MV_API int mv_ep_unpack(const void* recv_rows, int H, int world, int cap, int NK, int* ids, float* wts, void* stream);
 MV_API int mv_ep_combine(const void* x, long long x_stride, const float* y_local, const float* back, const int* pos,
                          int N, int K, int H, void* out, void* stream);
 

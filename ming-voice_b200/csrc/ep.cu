@@ -1,6 +1,6 @@
 // Expert-parallel prefill: the device side of one rank's dispatch and combine (the exchange itself is two NCCL
-// all-to-alls of fixed size issued by the host; nothing here synchronises the host, so a whole step can be
-// captured in a CUDA graph).
+// all-to-alls of fixed size issued by the host, rows out and fp32 outputs back; nothing here synchronises the
+// host).
 //
 // Placement (ming-voice is single-GPU, engine.py:34; expert parallelism is new): every rank holds the router,
 // the norm, the shared-expert slots and the replicated hot experts; each other ("cold") expert lives on one rank.
@@ -13,8 +13,10 @@
 //                   per-owner (slot, weight) metadata with the count in entry cap of each block, the source token
 //                   of each place, and pos[n, k] = d * cap + j (-1 for local pairs). More than cap pairs for one
 //                   owner: the excess pairs are dropped and the capacity error is raised in the workspace.
-//   mv_ep_pack      rows of the normalised tokens into the send blocks (one warp per place in use).
-//   mv_ep_unpack    received metadata -> ids / weights of the received rows (id -1 for unused places).
+//   mv_ep_pack      rows of the normalised tokens into the send blocks (one warp per place). A wire row is the H
+//                   bf16 values and a 16-byte tail (slot, weight, in-use flag), so rows and their metadata cross
+//                   in ONE all-to-all; a place past the count gets only its tail (flag 0).
+//   mv_ep_unpack    received tails -> ids / weights of the received rows (id -1 for unused places).
 //   mv_ep_combine   out[n] = bf16(x[n] + y_local[n] + sum over n's remote pairs, in k order, of their returned
 //                   fp32 outputs): one rounding, the same sum as one GPU computes.
 #include <cuda_runtime.h>
@@ -28,6 +30,10 @@ namespace ep {
 constexpr int kMaxWorld = 8;
 constexpr int kPlanThreads = 1024;
 
+// STAGED: the routed ids and the owner table are first copied into shared memory (coalesced), so the two
+// per-thread passes over contiguous pair ranges (which keep the token order) read shared memory, not scattered
+// global words.
+template <bool STAGED>
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restrict__ ids, const float* __restrict__ wts,
                                                             int N, int NK, int K, const int* __restrict__ owner,
                                                             const int* __restrict__ slot, int E, int rank, int world,
@@ -37,18 +43,27 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
                                                             WsHeader* ws) {
   __shared__ int s_warp[kPlanThreads / 32][kMaxWorld];
   __shared__ int s_base[kMaxWorld];
+  extern __shared__ int s_dyn[];  // STAGED: [E] owner, [N * K] routed ids
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const long long P = static_cast<long long>(N) * K;
   const long long chunk = (P + kPlanThreads - 1) / kPlanThreads;
   const long long p0 = chunk * t, p1 = min(P, p0 + chunk);
+  int* s_owner = s_dyn;
+  int* s_ids = s_dyn + E;
+  if (STAGED) {
+    for (int e = t; e < E; e += kPlanThreads) s_owner[e] = owner[e];
+    for (long long q = t; q < P; q += kPlanThreads) s_ids[q] = ids[(q / K) * NK + q % K];
+    __syncthreads();
+  }
+  auto id_at = [&](long long q) { return STAGED ? s_ids[q] : ids[(q / K) * NK + q % K]; };
+  auto owner_of = [&](int e) { return STAGED ? s_owner[e] : owner[e]; };
   // pass 1: this thread's pairs per owner
   int cnt[kMaxWorld];
 #pragma unroll
   for (int d = 0; d < kMaxWorld; ++d) cnt[d] = 0;
   for (long long q = p0; q < p1; ++q) {
-    const int n = static_cast<int>(q / K), k = static_cast<int>(q % K);
-    const int e = ids[static_cast<long long>(n) * NK + k];
-    const int d = (e >= 0 && e < E) ? owner[e] : -1;
+    const int e = id_at(q);
+    const int d = (e >= 0 && e < E) ? owner_of(e) : -1;
     if (d >= 0 && d != rank) {
 #pragma unroll
       for (int dd = 0; dd < kMaxWorld; ++dd) cnt[dd] += dd == d ? 1 : 0;
@@ -90,8 +105,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
   for (long long q = p0; q < p1; ++q) {
     const int n = static_cast<int>(q / K), k = static_cast<int>(q % K);
     const long long iq = static_cast<long long>(n) * NK + k;
-    const int e = ids[iq];
-    const int d = (e >= 0 && e < E) ? owner[e] : rank;
+    const int e = id_at(q);
+    const int d = (e >= 0 && e < E) ? owner_of(e) : rank;
     int pq = -1;
     if (e >= 0 && e < E && d != rank && d >= 0) {
       int j = 0;
@@ -123,35 +138,43 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
   if (t < world) send_meta[(static_cast<long long>(t) * (cap + 1) + cap) * 2] = min(s_base[t], cap);
 }
 
-// one warp per send place (d, j): row send_src[d, j] of xn -> send_rows[d * cap + j] (places past the count skip)
+// one warp per send place (d, j): row send_src[d, j] of xn and its tail -> wire row d * cap + j of send_rows
+// (row stride H + 8 elements); a place past the count gets only a tail with flag 0
 __global__ void __launch_bounds__(256) pack_kernel(const uint16_t* __restrict__ xn, long long x_stride, int H,
                                                    const int* __restrict__ send_src, const int* __restrict__ send_meta,
                                                    int world, int cap, uint16_t* __restrict__ send_rows) {
   const int lane = threadIdx.x & 31;
   const long long total = static_cast<long long>(world) * cap;
+  const int HW = H + 8;
   for (long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < total;
        w += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
     const int d = static_cast<int>(w / cap), j = static_cast<int>(w % cap);
-    if (j >= send_meta[(static_cast<long long>(d) * (cap + 1) + cap) * 2]) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(xn + static_cast<long long>(send_src[w]) * x_stride);
-    uint4* dst = reinterpret_cast<uint4*>(send_rows + w * H);
-    for (int v = lane; v < H / 8; v += 32) dst[v] = src[v];
+    const bool used = j < send_meta[(static_cast<long long>(d) * (cap + 1) + cap) * 2];
+    uint4* dst = reinterpret_cast<uint4*>(send_rows + w * HW);
+    if (used) {
+      const uint4* src = reinterpret_cast<const uint4*>(xn + static_cast<long long>(send_src[w]) * x_stride);
+      for (int v = lane; v < H / 8; v += 32) dst[v] = src[v];
+    }
+    if (lane == 0) {
+      const long long m = (static_cast<long long>(d) * (cap + 1) + j) * 2;
+      dst[H / 8] = used ? make_uint4(static_cast<uint32_t>(send_meta[m]), static_cast<uint32_t>(send_meta[m + 1]), 1u, 0u)
+                        : make_uint4(0u, 0u, 0u, 0u);
+    }
   }
 }
 
-// received places -> ids / weights of the received rows: column 0 the pair, the other columns -1
-__global__ void __launch_bounds__(256) unpack_kernel(const int* __restrict__ recv_meta, int world, int cap, int NK,
-                                                     int* __restrict__ ids, float* __restrict__ wts) {
-  const long long total = static_cast<long long>(world) * cap * NK;
+// received wire rows' tails -> ids / weights of the received rows: column 0 the pair, the other columns -1
+__global__ void __launch_bounds__(256) unpack_kernel(const uint16_t* __restrict__ recv_rows, int H, long long rows,
+                                                     int NK, int* __restrict__ ids, float* __restrict__ wts) {
+  const long long total = rows * NK;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long row = i / NK;
     const int col = static_cast<int>(i % NK);
-    const int d = static_cast<int>(row / cap), j = static_cast<int>(row % cap);
-    const long long m = (static_cast<long long>(d) * (cap + 1) + j) * 2;
-    const bool valid = col == 0 && j < recv_meta[(static_cast<long long>(d) * (cap + 1) + cap) * 2];
-    ids[i] = valid ? recv_meta[m] : -1;
-    wts[i] = valid ? __int_as_float(recv_meta[m + 1]) : 0.f;
+    const uint4 tail = reinterpret_cast<const uint4*>(recv_rows + row * (H + 8))[H / 8];
+    const bool valid = col == 0 && tail.z == 1u;
+    ids[i] = valid ? static_cast<int>(tail.x) : -1;
+    wts[i] = valid ? __uint_as_float(tail.y) : 0.f;
   }
 }
 
@@ -202,9 +225,20 @@ extern "C" int mv_ep_plan(const int* ids, const float* wts, int N, int NK, int K
   if (N < 0 || K < 1 || NK < K || E < 1 || cap < 1) return fail(MV_ERR_INVALID, "mv_ep_plan: bad shape");
   if (workspace == nullptr || workspace_bytes < kWsHeaderBytes)
     return fail(MV_ERR_WORKSPACE, "mv_ep_plan: workspace of %zu bytes needed", kWsHeaderBytes);
-  ep::plan_kernel<<<1, ep::kPlanThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      ids, wts, N, NK, K, owner, slot, E, rank, world, cap, ids_local, wts_local, pos, send_src, send_meta,
-      static_cast<WsHeader*>(workspace));
+  const size_t dyn = (static_cast<size_t>(E) + static_cast<size_t>(N) * K) * sizeof(int);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dyn <= 200 * 1024) {  // ids and owner table staged in shared memory
+    cudaError_t e = cudaFuncSetAttribute(ep::plan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(dyn));
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(ep plan)");
+    ep::plan_kernel<true><<<1, ep::kPlanThreads, dyn, st>>>(ids, wts, N, NK, K, owner, slot, E, rank, world, cap,
+                                                            ids_local, wts_local, pos, send_src, send_meta,
+                                                            static_cast<WsHeader*>(workspace));
+  } else {
+    ep::plan_kernel<false><<<1, ep::kPlanThreads, 0, st>>>(ids, wts, N, NK, K, owner, slot, E, rank, world, cap,
+                                                           ids_local, wts_local, pos, send_src, send_meta,
+                                                           static_cast<WsHeader*>(workspace));
+  }
   return cuda_status(cudaGetLastError(), "mv_ep_plan launch");
 }
 
@@ -214,6 +248,7 @@ extern "C" int mv_ep_pack(const void* xn, long long x_stride, int H, const int* 
     return fail(MV_ERR_INVALID, "mv_ep_pack: null pointer argument");
   if (H % 8 || x_stride % 8 || !aligned16(xn) || !aligned16(send_rows))
     return fail(MV_ERR_ALIGN, "mv_ep_pack: 16-byte aligned rows needed");
+  if (world < 1 || cap < 1) return fail(MV_ERR_INVALID, "mv_ep_pack: bad world / cap");
   const long long warps = static_cast<long long>(world) * cap;
   const unsigned int blocks = static_cast<unsigned int>((warps + 7) / 8 < 148 * 8 ? (warps + 7) / 8 : 148 * 8);
   ep::pack_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -222,12 +257,15 @@ extern "C" int mv_ep_pack(const void* xn, long long x_stride, int H, const int* 
   return cuda_status(cudaGetLastError(), "mv_ep_pack launch");
 }
 
-extern "C" int mv_ep_unpack(const int* recv_meta, int world, int cap, int NK, int* ids, float* wts, void* stream) {
-  if (recv_meta == nullptr || ids == nullptr || wts == nullptr) return fail(MV_ERR_INVALID, "mv_ep_unpack: null");
-  const long long total = static_cast<long long>(world) * cap * NK;
+extern "C" int mv_ep_unpack(const void* recv_rows, int H, int world, int cap, int NK, int* ids, float* wts,
+                            void* stream) {
+  if (recv_rows == nullptr || ids == nullptr || wts == nullptr) return fail(MV_ERR_INVALID, "mv_ep_unpack: null");
+  if (H % 8 || !aligned16(recv_rows)) return fail(MV_ERR_ALIGN, "mv_ep_unpack: 16-byte aligned wire rows needed");
+  const long long rows = static_cast<long long>(world) * cap;
+  const long long total = rows * NK;
   const unsigned int blocks = static_cast<unsigned int>((total + 255) / 256 < 148 * 4 ? (total + 255) / 256 : 148 * 4);
-  ep::unpack_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(recv_meta, world, cap, NK,
-                                                                                              ids, wts);
+  ep::unpack_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(recv_rows), H, rows, NK, ids, wts);
   return cuda_status(cudaGetLastError(), "mv_ep_unpack launch");
 }
 

@@ -174,7 +174,10 @@ __global__ void __launch_bounds__(kChunk) align_scatter_kernel(const void* __res
 // ------------------------------------------------------------------------------------------------ gather
 
 // One warp per row: rows [0, nb_used*128) of xs from the sorted pairs, then rows [0, N) of y32.
-__global__ void __launch_bounds__(256) gather_kernel(const uint16_t* __restrict__ x, long long x_stride,
+// Rows [0, n_x) of the pass come from x, rows [n_x, N) from x2 (row stride x2_stride): the own and the received
+// rows of an expert-parallel pass, read where they lie.
+__global__ void __launch_bounds__(256) gather_kernel(const uint16_t* __restrict__ x, long long x_stride, int n_x,
+                                                     const uint16_t* __restrict__ x2, long long x2_stride,
                                                      const int* __restrict__ sorted, const int* __restrict__ nb_used,
                                                      int NK, int P, int H, uint16_t* __restrict__ xs,
                                                      const uint16_t* __restrict__ residual, long long r_stride,
@@ -192,7 +195,9 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint16_t* __restrict_
       const int p = sorted[row];
       uint4* dst = reinterpret_cast<uint4*>(xs + row * H);
       if (p < P) {
-        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<long long>(p / NK) * x_stride);
+        const int tok = p / NK;
+        const uint4* src = reinterpret_cast<const uint4*>(
+            tok < n_x ? x + static_cast<long long>(tok) * x_stride : x2 + static_cast<long long>(tok - n_x) * x2_stride);
         for (int v = lane; v < nv; v += 32) dst[v] = src[v];
       } else {
         for (int v = lane; v < nv; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
@@ -665,7 +670,11 @@ extern "C" size_t mv_moe_prefill_workspace_bytes(int N, int NK, int H, int I, in
 // (residual added in fp32 when given) and nothing is rounded to bf16.
 static int prefill_run(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids, int ids_dtype,
                        const float* wts, int N, int NK, const void* residual, long long residual_stride, void* out,
-                       float* out32, void* workspace, size_t workspace_bytes, void* stream) {
+                       float* out32, void* workspace, size_t workspace_bytes, void* stream, int max_ctas = 0,
+                       int n_x = -1, const void* x2 = nullptr, long long x2_stride = 0) {
+  if (n_x < 0 || x2 == nullptr) n_x = N;
+  if (n_x < N && (!aligned16(x2) || (x2_stride * 2) % 16 || x2_stride < w->H))
+    return fail(MV_ERR_ALIGN, "mv_moe_prefill: second row source must be 16-byte aligned with a row stride >= H");
   if (w == nullptr || (N > 0 && (x == nullptr || ids == nullptr || wts == nullptr || (out == nullptr && out32 == nullptr))))
     return fail(MV_ERR_INVALID, "mv_moe_prefill: null pointer argument");
   if (ids_dtype != MV_I32 && ids_dtype != MV_I64) return fail(MV_ERR_INVALID, "mv_moe_prefill: ids must be i32 or i64");
@@ -739,8 +748,9 @@ static int prefill_run(const mv_moe_weights* w, const void* x, long long x_strid
   if ((rc = launch_align(ids, ids_dtype, L.P, E1, kBM, L.nb_max, sorted, bexp, nb_used,
                         reinterpret_cast<int*>(ws + L.off_align), hdr, st)) != MV_OK)
     return rc;
-  const int G = num_sms();
-  gather_kernel<<<G * 4, 256, 0, st>>>(static_cast<const uint16_t*>(x), x_stride, sorted, nb_used, NK, L.P, H, xs,
+  const int G = max_ctas > 0 && max_ctas < num_sms() ? max_ctas : num_sms();  // SMs for the persistent GEMM
+  gather_kernel<<<G * 4, 256, 0, st>>>(static_cast<const uint16_t*>(x), x_stride, n_x,
+                                       static_cast<const uint16_t*>(x2), x2_stride, sorted, nb_used, NK, L.P, H, xs,
                                        static_cast<const uint16_t*>(residual), residual_stride, y32, N, ready,
                                        L.nb_max);
   cudaError_t e = cudaGetLastError();
@@ -809,11 +819,13 @@ extern "C" int mv_moe_prefill(const mv_moe_weights* w, const void* x, long long 
                      workspace_bytes, stream);
 }
 
-extern "C" int mv_moe_prefill_f32(const mv_moe_weights* w, const void* x, long long x_stride, const void* ids,
-                                  int ids_dtype, const float* wts, int N, int NK, const void* residual,
-                                  long long residual_stride, float* out32, void* workspace, size_t workspace_bytes,
-                                  void* stream) {
+extern "C" int mv_moe_prefill_f32(const mv_moe_weights* w, const void* x, long long x_stride, int n_x,
+                                  const void* x2, long long x2_stride, const void* ids, int ids_dtype, const float* wts,
+                                  int N, int NK, const void* residual, long long residual_stride, float* out32,
+                                  int max_ctas, void* workspace, size_t workspace_bytes, void* stream) {
   if (out32 == nullptr && N > 0) return fail(MV_ERR_INVALID, "mv_moe_prefill_f32: null pointer argument");
+  if (max_ctas < 0 || n_x < 0 || n_x > N || (n_x < N && x2 == nullptr))
+    return fail(MV_ERR_INVALID, "mv_moe_prefill_f32: bad max_ctas / n_x / second row source");
   return prefill_run(w, x, x_stride, ids, ids_dtype, wts, N, NK, residual, residual_stride, nullptr, out32, workspace,
-                     workspace_bytes, stream);
+                     workspace_bytes, stream, max_ctas, n_x, x2, x2_stride);
 }

@@ -69,11 +69,12 @@ _SIGS = {
     "mv_moe_prefill_workspace_bytes": (SZ, [I32, I32, I32, I32, I32, I32]),
     "mv_quantize_into_stack": (I32, [P, I32, I64, I32, I32, P, P, I32, I32, I32, I32, I32, P]),
     "mv_mask_pad_rows": (I32, [P, I32, I32, I32, P, P]),
-    "mv_moe_prefill_f32": (I32, [C.POINTER(MoeWeights), P, I64, P, I32, P, I32, I32, P, I64, P, P, SZ, P]),
+    "mv_moe_prefill_f32": (I32, [C.POINTER(MoeWeights), P, I64, I32, P, I64, P, I32, P, I32, I32, P, I64, P, I32, P,
+                                 SZ, P]),
     "mv_ep_workspace_bytes": (SZ, []),
     "mv_ep_plan": (I32, [P, P, I32, I32, I32, P, P, I32, I32, I32, I32, P, P, P, P, P, P, SZ, P]),
     "mv_ep_pack": (I32, [P, I64, I32, P, P, I32, I32, P, P]),
-    "mv_ep_unpack": (I32, [P, I32, I32, I32, P, P, P]),
+    "mv_ep_unpack": (I32, [P, I32, I32, I32, I32, P, P, P]),
     "mv_ep_combine": (I32, [P, I64, P, P, P, I32, I32, I32, P, P]),
 }
 

@@ -8,17 +8,16 @@ replicating them costs 17 MB per expert of the 180 GB on each GPU.
 
 A prefill step on a rank's own packed tokens (CUDA path, no host synchronisation anywhere: the exchange has a
 fixed capacity `cap` of pairs per peer, so the step can be captured in a CUDA graph):
-  1. RMSNorm and routing locally (mv_rmsnorm, mv_route), the normalised rows written into the first N rows of one
-     [N + world * cap, H] buffer;
+  1. RMSNorm and routing locally (mv_rmsnorm, mv_route);
   2. mv_ep_plan (one CTA) gives every pair whose expert lives here its local slot and every other pair a place in
-     its owner's send block (token order kept), mv_ep_pack copies those rows into the send blocks;
-  3. two NCCL all-to-alls of fixed size: the (slot, weight) metadata with each block's count, and the rows, which
-     land in the last world * cap rows of the buffer (the one exchange step of the block);
-  4. ONE tcgen05 grouped-GEMM pass (mv_moe_prefill_f32) over the own rows (local pairs; the rest -1, skipped by the
-     expert sort) and the received rows (their one pair; unused places -1), fp32 outputs;
-  5. the received rows' fp32 outputs go back with one more all-to-all and mv_ep_combine adds, per token, the
-     residual, the local sum and its remote pairs' outputs in pair order, rounding once to bf16 -- the same sum a
-     single GPU makes.
+     its owner's send block (token order kept); mv_ep_pack writes those rows into the send blocks as wire rows
+     (H values and a 16-byte (slot, weight, in-use) tail);
+  3. one NCCL all-to-all of fixed size moves the wire rows (the one exchange step of the block);
+  4. ONE tcgen05 grouped-GEMM pass (mv_moe_prefill_f32, fp32 outputs) over the own rows (local pairs; the rest -1,
+     skipped by the expert sort) and the received rows where they landed (their one pair; unused places -1);
+     the received rows' outputs go back with a second all-to-all;
+  5. mv_ep_combine adds, per token, the residual, the local sum and its remote pairs' outputs in pair order,
+     rounding once to bf16 -- the same sum a single GPU makes.
 More than `cap` pairs for one peer is an error recorded in the plan's workspace (the excess pairs are dropped);
 `plan_capacity` measures what a batch needs. No kernel reads another GPU's memory: everything remote arrives
 through NCCL. With an `experts_fn` (the CPU tests) the same step runs on torch tensors with data-dependent
@@ -119,17 +118,17 @@ class EPMoeBlock:
             b, W = self.block, self.world
             R, NK, H = W * cap, b.nk, b.H
             bf = dict(
-                xall=torch.empty(N + R, H, dtype=torch.bfloat16, device=dev),
+                xn=torch.empty(N, H, dtype=torch.bfloat16, device=dev),
                 ids=torch.empty(N, NK, dtype=torch.int32, device=dev),
                 wts=torch.empty(N, NK, dtype=torch.float32, device=dev),
                 logits=torch.empty(N, b.E, dtype=torch.float32, device=dev),
-                ids_all=torch.empty(N + R, NK, dtype=torch.int32, device=dev),
+                ids_all=torch.empty(N + R, NK, dtype=torch.int32, device=dev),  # own rows, then received rows
                 wts_all=torch.empty(N + R, NK, dtype=torch.float32, device=dev),
                 pos=torch.empty(N, b.top_k, dtype=torch.int32, device=dev),
                 send_src=torch.zeros(R, dtype=torch.int32, device=dev),
                 send_meta=torch.zeros(W, cap + 1, 2, dtype=torch.int32, device=dev),
-                recv_meta=torch.zeros(W, cap + 1, 2, dtype=torch.int32, device=dev),
-                send_rows=torch.zeros(R, H, dtype=torch.bfloat16, device=dev),
+                send_rows=torch.zeros(R, H + 8, dtype=torch.bfloat16, device=dev),  # wire rows: H values + tail
+                recv_rows=torch.zeros(R, H + 8, dtype=torch.bfloat16, device=dev),
                 y32=torch.empty(N + R, H, dtype=torch.float32, device=dev),
                 back=torch.empty(R, H, dtype=torch.float32, device=dev),
                 out=torch.empty(N, H, dtype=torch.bfloat16, device=dev),
@@ -154,8 +153,7 @@ class EPMoeBlock:
         bf = self._buffers(N, cap, dev)
         st = L.stream_ptr(dev)
         lib = L.lib()
-        xall = bf["xall"]
-        xn = xall[:N]
+        xn = bf["xn"]
         if b.norm_w is not None:
             L.check(lib.mv_rmsnorm(L.ptr(x), L.MV_BF16, x.stride(0), L.ptr(b.norm_w), L.MV_BF16, L.ptr(xn), L.MV_BF16,
                                    N, H, C.c_float(b.eps), st), "mv_rmsnorm")
@@ -165,25 +163,28 @@ class EPMoeBlock:
                             bf["ids"], bf["wts"], mode=b.route_mode, n_shared=len(b.shared_ids),
                             shared_id=b.shared_ids[0] if b.shared_ids else b.E, w_scale=b.router_s)
         ws = L.workspace("ep", int(lib.mv_ep_workspace_bytes()), dev)
+        ids_all, wts_all = bf["ids_all"], bf["wts_all"]
         L.check(lib.mv_ep_plan(L.ptr(bf["ids"]), L.ptr(bf["wts"]), N, NK, K, L.ptr(bf["owner"]), L.ptr(bf["slot"]),
-                               self.E, self.rank, W, cap, L.ptr(bf["ids_all"]), L.ptr(bf["wts_all"]), L.ptr(bf["pos"]),
+                               self.E, self.rank, W, cap, L.ptr(ids_all), L.ptr(wts_all), L.ptr(bf["pos"]),
                                L.ptr(bf["send_src"]), L.ptr(bf["send_meta"]), L.ptr(ws), ws.numel(), st), "mv_ep_plan")
-        L.check(lib.mv_ep_pack(L.ptr(xn), xn.stride(0), H, L.ptr(bf["send_src"]), L.ptr(bf["send_meta"]), W, cap,
+        L.check(lib.mv_ep_pack(L.ptr(xn), H, H, L.ptr(bf["send_src"]), L.ptr(bf["send_meta"]), W, cap,
                                L.ptr(bf["send_rows"]), st), "mv_ep_pack")
-        dist.all_to_all_single(bf["recv_meta"], bf["send_meta"], group=self.group)
-        dist.all_to_all_single(xall[N:], bf["send_rows"], group=self.group)
-        L.check(lib.mv_ep_unpack(L.ptr(bf["recv_meta"]), W, cap, NK, L.ptr(bf["ids_all"][N:]),
-                                 L.ptr(bf["wts_all"][N:]), st), "mv_ep_unpack")
+        # the exchange: rows and their (slot, weight) tails in one all-to-all
+        dist.all_to_all_single(bf["recv_rows"], bf["send_rows"], group=self.group)
+        L.check(lib.mv_ep_unpack(L.ptr(bf["recv_rows"]), H, W, cap, NK, L.ptr(ids_all[N:]), L.ptr(wts_all[N:]), st),
+                "mv_ep_unpack")
+        # one grouped-GEMM pass: own rows from xn, received rows where they landed (wire row stride H + 8)
         wst = moe.weights_struct(b.w_gu, b.w_d, b.s_gu, b.s_d)
         nbytes = lib.mv_moe_prefill_workspace_bytes(N + R, NK, H, b.I, b.w_gu.shape[0], L.dt(b.w_gu))
         pws = L.workspace("prefill", nbytes, dev)
-        L.check(lib.mv_moe_prefill_f32(C.byref(wst), L.ptr(xall), H, L.ptr(bf["ids_all"]), L.MV_I32,
-                                       L.ptr(bf["wts_all"]), N + R, NK, None, 0, L.ptr(bf["y32"]), L.ptr(pws),
+        y32 = bf["y32"]
+        L.check(lib.mv_moe_prefill_f32(C.byref(wst), L.ptr(xn), H, N, L.ptr(bf["recv_rows"]), H + 8, L.ptr(ids_all),
+                                       L.MV_I32, L.ptr(wts_all), N + R, NK, None, 0, L.ptr(y32), 0, L.ptr(pws),
                                        pws.numel(), st), "mv_moe_prefill_f32")
-        dist.all_to_all_single(bf["back"], bf["y32"][N:], group=self.group)
+        dist.all_to_all_single(bf["back"], y32[N:], group=self.group)
         out = bf["out"]
-        L.check(lib.mv_ep_combine(L.ptr(x), x.stride(0), L.ptr(bf["y32"]), L.ptr(bf["back"]), L.ptr(bf["pos"]), N, K,
-                                  H, L.ptr(out), st), "mv_ep_combine")
+        L.check(lib.mv_ep_combine(L.ptr(x), x.stride(0), L.ptr(y32), L.ptr(bf["back"]), L.ptr(bf["pos"]), N, K, H,
+                                  L.ptr(out), st), "mv_ep_combine")
         return out
 
     def errors(self):
