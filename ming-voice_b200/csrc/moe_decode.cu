@@ -895,11 +895,10 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
   const size_t lg = (static_cast<size_t>(M) * (p.router ? p.E : 0) * 4 + 255) & ~size_t(255);
   p.logits_ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes);
   p.a_g = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes + lg);
-  {  // one token with the router fused, int8 weights: the dedicated kernel (moe_decode_m1.cu: 42.6 vs 44.0 us per
-    // block in the 16-layer graph; for bf16 this kernel measured 48.8 us against 44.9, so bf16 runs it only with
-    // MINGMOE_DECODE_PATH=m1, and =classic keeps int8 here too)
+  {  // one token with the router fused: the dedicated kernel (moe_decode_m1.cu; MINGMOE_DECODE_PATH=classic keeps
+    // this kernel)
     const char* path = getenv("MINGMOE_DECODE_PATH");
-    const bool want = path != nullptr ? path[0] == 'm' : int8;
+    const bool want = path == nullptr || path[0] == 'm';
     if (M == 1 && p.router && want) {
       const int rc = decode_m1_run(p, int8, st);
       if (rc != kDecodeM1Unsuitable) return rc;

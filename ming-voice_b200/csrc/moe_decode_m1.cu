@@ -22,7 +22,14 @@
 //  * Routing: the shared-expert (static) rows need no routing, so the first ring-full of them is copied at
 //    kernel entry and consumed while the router runs: warp w of CTA b computes the logit of expert w * G + b
 //    (fp64 dot, rounded once to fp32), a grid barrier publishes them, and every CTA makes the same selection
-//    (one warp, ties to the lower id) and builds its expert table.
+//    with all its threads (route::select_parallel: every expert's rank among the biased scores, ties to the
+//    lower id, so no serial rounds of arg-max; the router bias was staged in shared memory at entry) and writes
+//    its one-token expert table directly (static slots, then the picks in id order). The selection sits on the
+//    critical path of every block: made by one warp it took ~3 us of the block's ~48, made by the CTA well
+//    under one, and the whole block ran at 39.6 us instead of 48.1 (bf16) and 40.0 instead of 43.1 (int8).
+//    Two L2 prefetches of the down rows measured slower and are not used: issued at the routing decision
+//    (43.6 us) they delay the routed gate/up stream, issued at the end of the gate/up phase (42.1 us) they
+//    delay the slowest CTAs on the grid barrier, and neither shortened the down phase.
 //
 // Numerics: as moe_decode.cu (fp32 accumulation and intermediates; int8 dequantised element by element as
 // float(q) * float(scale), torch's dequantisation; RMSNorm as mv_rmsnorm).
@@ -43,8 +50,8 @@ constexpr int kThreads = kWarps * 32;
 
 // Shared-memory layout (byte offsets), computed identically on the host (size check) and the device.
 struct Layout {
-  unsigned int bars, xn, abuf, gsc, dsc, e_id, e_ntok, e_pbase, e_tok, e_w, misc, pr_e, pr_w, sel_r, sel_sc, red,
-      gpart, ypart, total;
+  unsigned int bars, xn, abuf, gsc, dsc, e_id, e_ntok, e_pbase, e_tok, e_w, misc, pr_e, pr_w, sel_r, sel_sc, sel_k,
+      sbias, red, gpart, ypart, total;
 };
 
 __host__ __device__ inline unsigned int take(unsigned int& o, unsigned int bytes, unsigned int align) {
@@ -72,6 +79,8 @@ __host__ __device__ inline Layout layout(int H, int I, int E, int u_max, int nhc
   L.pr_w = take(o, kMaxNK * 4, 4);
   L.sel_r = take(o, E * 4, 16);
   L.sel_sc = take(o, E * 4, 16);
+  L.sel_k = take(o, kMaxNK * 8 + 32 * 4, 16);                 // selection: pick values (fp64), group scores
+  L.sbias = take(o, E * 4, 16);                               // the router bias, loaded at the start
   L.red = take(o, kWarps * 8, 8);
   L.gpart = take(o, kGroups * 2 * 2 * RG * kGW * 4, 16);
   L.ypart = take(o, u_max * nhc * kGW * 4, 16);
@@ -132,6 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
   float* pr_w = reinterpret_cast<float*>(smem + Lo.pr_w);
   float* sel_r = reinterpret_cast<float*>(smem + Lo.sel_r);
   float* sel_sc = reinterpret_cast<float*>(smem + Lo.sel_sc);
+  double* sel_kd = reinterpret_cast<double*>(smem + Lo.sel_k);
+  float* sel_gs = reinterpret_cast<float*>(smem + Lo.sel_k + kMaxNK * 8);
+  float* sbias = reinterpret_cast<float*>(smem + Lo.sbias);
   double* red = reinterpret_cast<double*>(smem + Lo.red);
   float* gpart = reinterpret_cast<float*>(smem + Lo.gpart);  // [group][2][2 RG][kGW]
   float* ypart = reinterpret_cast<float*>(smem + Lo.ypart);  // [u_max][nh_cap][kGW]
@@ -227,6 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
   if (lane == 0 && e_logit < p.E)
     bulk_prefetch_l2(static_cast<const uint8_t*>(p.rw) + static_cast<size_t>(e_logit) * H * resz,
                      static_cast<uint32_t>(H * resz));
+  // the router bias into shared memory now: the selection reads it on the critical path, long after this load
+  if (p.rbias != nullptr)
+    for (int j = tid; j < p.E; j += kThreads) sbias[j] = p.rbias[j];
   // this thread's output element's residual (the token itself), read now rather than at the end
   const float res_pre =
       (p.residual != nullptr && tid < nh) ? __uint_as_float(static_cast<uint32_t>(p.residual[hd0 + tid]) << 16) : 0.f;
@@ -390,15 +405,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
   // ---- routing: every CTA makes the same selection from the published logits (one warp), then its table
   if (tid == 0) grid_wait_gen(&p.ws->gen1, tgt1, p.ws, 0x300u);
   if (tid == 0) MV_TRACE_AT(p, 3);
+  if (tid < kMaxNK) pr_e[tid] = -1;  // a pick the selection leaves unset stays invalid
   named_bar(1, kThreads);
+  {  // the selection by all threads: ranks instead of rounds of arg-max (the same picks, ties to the lower id)
+    const route::SelectCfg cfg{p.route_mode, p.E, p.top_k, p.n_group, p.topk_group, p.rscale,
+                               p.rbias != nullptr ? sbias : nullptr};
+    route::select_parallel(cfg, p.logits_ws, 1, tid, kThreads, [] { named_bar(1, kThreads); }, sel_r, sel_sc, sel_kd,
+                           sel_gs, pr_e, pr_w);
+  }
+  if (tid == 0) MV_TRACE_AT(p, 15);
   if (warp == 0) {
-    for (int j = lane; j < p.E; j += 32) sel_r[j] = ld_cg_f32(p.logits_ws + j);
-    __syncwarp();
-    if (tid == 0) MV_TRACE_AT(p, 14);
-    const route::SelectCfg cfg{p.route_mode, p.E, p.top_k, p.n_group, p.topk_group, p.rscale, p.rbias};
-    route::select_core(cfg, sel_r, sel_sc, pr_e, pr_w);
-    __syncwarp();
-    if (tid == 0) MV_TRACE_AT(p, 15);
     if (blockIdx.x == 0) {  // router outputs: ids / weights with the static slots appended, logits
       const int NKT = p.top_k + n_static;
       for (int k = lane; k < NKT; k += 32) {
@@ -412,16 +428,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
         if (p.wts_out) p.wts_out[k] = k < p.top_k ? pr_w[k] : 1.0f;
       }
       if (p.logits_out)
-        for (int j = lane; j < p.E; j += 32) p.logits_out[j] = sel_r[j];
+        for (int j = lane; j < p.E; j += 32) p.logits_out[j] = ld_cg_f32(p.logits_ws + j);
     }
     if (tid == 0) MV_TRACE_AT(p, 16);
-    table_warp<1>(pr_e, pr_w, p.top_k, p.top_k, p.E1, n_static, p.static_id, 1, e_id, e_ntok, e_tok, e_w, e_pbase,
-                  misc, p.ws);
+    {  // the expert table of one token: the static slots, then the valid picks (distinct experts) in id order
+      const int K = p.top_k;
+      const int pe = lane < K ? pr_e[lane] : -1;
+      const bool valid = pe >= 0 && pe < p.E1;
+      const int e = valid ? pe : 0x7fffffff;
+      const float w = valid ? pr_w[lane] : 0.f;
+      int rank = n_static;
+      for (int j = 0; j < K; ++j) rank += __shfl_sync(0xffffffffu, e, j) < e ? 1 : 0;
+      if (valid) {
+        e_id[rank] = e;
+        e_w[rank] = w;
+      }
+      const int Ut = n_static + __popc(__ballot_sync(0xffffffffu, valid));
+      for (int u = lane; u < Ut; u += 32) {
+        if (u < n_static) {
+          e_id[u] = p.static_id + u;
+          e_w[u] = 1.0f;
+        }
+        e_ntok[u] = 1;
+        e_tok[u] = 0;
+        e_pbase[u] = u;
+      }
+      if (lane == 0) {
+        misc[0] = Ut;
+        misc[3] = Ut;
+      }
+      __syncwarp();
+    }
     if (tid == 0) MV_TRACE_AT(p, 17);
   }
   named_bar(1, kThreads);
   if (tid == 0) MV_TRACE_AT(p, 4);
   const int U = misc[0];
+
   const long long T = S + static_cast<long long>(U - n_static) * I;
   r_lo = T * blockIdx.x / G - s_lo;
   r_hi = T * (blockIdx.x + 1) / G - s_hi;
@@ -493,7 +536,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
     have = hn;
   }
   if (tid == 0) MV_TRACE_AT(p, 6);
-
   // ---- grid barrier: every CTA's activations are in the workspace; then this CTA loads them all
   named_bar(1, kThreads);
   if (tid == 0) {
@@ -623,7 +665,7 @@ int decode_m1_run(decode::Params& p, bool int8, cudaStream_t st) {
     kern = int8 ? decode_m1_kernel<true, 1536, 512> : decode_m1_kernel<false, 1536, 512>;
   if (kern == nullptr) return kDecodeM1Unsuitable;
   const int G = num_sms();
-  if (p.E > kWarps * G || p.top_k > 32) return kDecodeM1Unsuitable;
+  if (p.E > kWarps * G || p.E > 128 || p.top_k > 32 || p.top_k > p.E) return kDecodeM1Unsuitable;
   const int RG = rows_per_stage(H * esz);
   p.RG = RG;
   p.u_max = p.n_static + (p.top_k < p.E ? p.top_k : p.E);
