@@ -226,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
     misc[0] = n_static;
   }
   __syncthreads();
+  pdl_launch_dependents();  // the next block's kernel may be scheduled now (it waits for this one to complete)
   if (issuer && grp < n_early) issue(early);
   // the next block's router rows and RMSNorm weight (its routing reads them first): one slice per CTA into L2
   if (tid == 32 && p.nx_rw != nullptr) {
@@ -242,6 +243,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
   // the router bias into shared memory now: the selection reads it on the critical path, long after this load
   if (p.rbias != nullptr)
     for (int j = tid; j < p.E; j += kThreads) sbias[j] = p.rbias[j];
+  // everything above reads weights only; the token and the workspace are the previous kernel's (a programmatic
+  // launch may start before it completes)
+  pdl_wait();
   // this thread's output element's residual (the token itself), read now rather than at the end
   const float res_pre =
       (p.residual != nullptr && tid < nh) ? __uint_as_float(static_cast<uint32_t>(p.residual[hd0 + tid]) << 16) : 0.f;
@@ -681,11 +685,19 @@ int decode_m1_run(decode::Params& p, bool int8, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  // programmatic launch: the kernel starts its weight copies while the previous kernel in the stream finishes
+  // (MINGMOE_PDL=0 turns it off)
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  static const bool pdl = [] {
+    const char* v = getenv("MINGMOE_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   e = cudaLaunchKernelEx(&cfg, kern, p);
   return cuda_status(e, "decode_m1 launch");
 }
