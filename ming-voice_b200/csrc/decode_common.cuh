@@ -4,6 +4,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "route_select.cuh"
@@ -379,6 +380,17 @@ __device__ void table_bitmap(const int* pr_e, const float* pr_w, int npairs, int
 // kDecodeTcUnsuitable when the shapes / workspace do not fit it (the caller then uses the CUDA-core kernel).
 constexpr int kDecodeTcUnsuitable = -1;
 constexpr int kDecodeM1Unsuitable = -2;
+
+// Whether the decode kernels are launched as programmatic dependents of the previous kernel in the stream (their
+// CTAs are scheduled while it finishes; each kernel waits for it before reading the token or the workspace).
+// MINGMOE_PDL=0 turns it off.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("MINGMOE_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
 int decode_m1_run(decode::Params& p, bool int8, cudaStream_t st);
 size_t decode_tc_workspace_bytes(int M, int nk, int H, int I, int E1, int E, int n_static);
 int decode_tc_run(decode::Params& p, void* workspace, size_t workspace_bytes, int nk_pairs, cudaStream_t st);

@@ -123,6 +123,8 @@ __global__ void __launch_bounds__(CW * 32 + 32, 1) moe_decode_kernel(const Param
     misc[1] = 0;
   }
   __syncthreads();
+  pdl_launch_dependents();  // the next kernel in the stream may be scheduled (it waits for this one)
+  pdl_wait();               // the tokens, pairs and workspace are the previous kernel's
 
   const int n_static = p.router ? p.n_static : 0;
   const long long S = static_cast<long long>(n_static) * I;
@@ -966,11 +968,13 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
   cfg.blockDim = dim3(CW * 32 + 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   e = cudaLaunchKernelEx(&cfg, kern, p);
   return cuda_status(e, "moe_decode launch");
 }

@@ -689,15 +689,10 @@ int decode_m1_run(decode::Params& p, bool int8, cudaStream_t st) {
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   // programmatic launch: the kernel starts its weight copies while the previous kernel in the stream finishes
-  // (MINGMOE_PDL=0 turns it off)
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
-  static const bool pdl = [] {
-    const char* v = getenv("MINGMOE_PDL");
-    return v == nullptr || v[0] != '0';
-  }();
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 2 : 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   e = cudaLaunchKernelEx(&cfg, kern, p);
   return cuda_status(e, "decode_m1 launch");
 }

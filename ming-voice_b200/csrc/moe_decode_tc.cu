@@ -252,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     misc[1] = 0;
     misc[2] = 0;
   }
+  pdl_launch_dependents();  // the next kernel in the stream may be scheduled (it waits for this one)
   if (warp == 0 && lane == 0) {
     tc::prefetch_tmap(&tm_gu);
     tc::prefetch_tmap(&tm_d);
@@ -265,6 +266,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int r_esz = p.rw_dtype == MV_F32 ? 4 : (p.rw_dtype == MV_BF16 ? 2 : 1);
   uint4 r_row[kRouterChunks];
   if (r_has) router_row_load(static_cast<const uint8_t*>(p.rw) + static_cast<size_t>(r_e) * H * r_esz, H * r_esz, r_row);
+  // the tokens, the workspace and (on this SM) the tensor memory are the previous kernel's until it completes
+  pdl_wait();
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tmem_relinquish();
@@ -946,11 +949,13 @@ int decode_tc_run(decode::Params& p, void* workspace, size_t workspace_bytes, in
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   e = cudaLaunchKernelEx(&cfg, moe_decode_tc_kernel, p, tm_gu, tm_d, tm_ab);
   return cuda_status(e, "moe_decode_tc launch");
 }

@@ -339,21 +339,48 @@ __device__ void select_parallel(const SelectCfg& p, const float* logits, int M, 
       }
     sync();
   }
-  for (int i = t; i < M * E; i += NT) {
+  // ranks: `per` consecutive threads (a power of two within a warp) share a candidate, each counting over every
+  // per-th competitor, and add their counts with shuffles; every thread runs the same number of rounds
+  const int ncand = M * E;
+  int per = 1;
+  while (per < 32 && per * 2 * ncand <= NT) per *= 2;
+  for (int base = 0; base < ncand * per; base += NT) {
+    const int i2 = base + t;
+    const bool act = i2 < ncand * per;
+    const int i = act ? i2 / per : 0, part = i2 % per;
     const int m = i / E, e = i % E;
     const float v = r_s[i];
-    const float* rr = r_s + m * E;
     int rank = 0;
-    for (int j = 0; j < E; ++j) {
-      const float o = rr[j];
-      rank += (o > v || (o == v && j < e)) ? 1 : 0;
+    if (act) {
+      const float* rr = r_s + m * E;
+      for (int j = part; j < E; j += per) {
+        const float o = rr[j];
+        rank += (o > v || (o == v && j < e)) ? 1 : 0;
+      }
     }
-    if (rank < K && v > -INFINITY) {
+    for (int o = per >> 1; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+    if (act && part == 0 && rank < K && v > -INFINITY) {
       sel_e[m * K + rank] = e;
       k_s[m * K + rank] = p.mode == MV_ROUTE_SIGMOID_GROUP ? static_cast<double>(sc_s[i]) : static_cast<double>(v);
     }
   }
   sync();
+  if (p.mode != MV_ROUTE_SIGMOID_GROUP && M * K <= NT) {
+    // softmax: each exponential once (exp(v_k - v_0), the rank-0 value is the maximum), then every weight sums
+    // the same values in the same order as below
+    const double ex = t < M * K ? exp(k_s[t] - k_s[(t / K) * K]) : 0.0;
+    sync();
+    if (t < M * K) k_s[t] = ex;
+    sync();
+    if (t < M * K) {
+      const double* kv = k_s + (t / K) * K;
+      double tot = 0.0;
+      for (int j = 0; j < K; ++j) tot += kv[j];
+      sel_w[t] = static_cast<float>(ex / tot);
+    }
+    sync();
+    return;
+  }
   for (int i = t; i < M * K; i += NT) {
     const int m = i / K, k = i % K;
     const double* kv = k_s + m * K;
