@@ -367,33 +367,51 @@ def ep_prefill_lines(dev, world, rank, steps, warmup):
     cap = ep.calibrate(x)  # the exchange capacity per peer, from this batch (before the timed region)
     for _ in range(warmup):
         ep.forward(x)
+    torch.cuda.synchronize()
+    # the step has no host synchronisation, so it is captured whole (NCCL all-to-alls included) in one CUDA graph,
+    # as the single-GPU pass is; every rank captures and replays the same collectives in the same order
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        ep.forward(x)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            ep.forward(x)
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    for _ in range(warmup):
+        graph.replay()
     torch.distributed.barrier()
     torch.cuda.synchronize()
     s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
     s_ev.record()
     for _ in range(steps):
-        ep.forward(x)
+        graph.replay()
     e_ev.record()
     torch.cuda.synchronize()
     t = torch.tensor([s_ev.elapsed_time(e_ev) / steps], dtype=torch.float64, device=dev)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     us = t.item() * 1e3
+    torch.distributed.barrier()
+    del graph  # a graph holding NCCL calls is released before the process group
     errs = ep.errors()
     if errs:
         raise RuntimeError(f"EP prefill device errors: {errs}")
     flops = O.prefill_flops(N) * world
     return {"tokens_per_gpu": N, "us_per_pass": round(us, 1), "tokens_per_s": round(world * N / us * 1e6, 0),
             "tflops": round(flops / us / 1e6, 1),
-            "parallelism": f"ep{world}: experts 0-{EP_REPLICATED - 1} replicated, {E - EP_REPLICATED} round-robin",
-            "exchange": f"NCCL all-to-all of fixed capacity {cap} pairs per peer: bf16 rows out, fp32 outputs back "
-                        "(device-side plan / pack / combine, no host synchronisation)", "flops_per_pass": flops}
+            "parallelism": f"ep{world}: experts 0-{EP_REPLICATED - 1} replicated, {E - EP_REPLICATED} dealt as a snake",
+            "exchange": f"NCCL all-to-all of fixed capacity {cap} pairs per peer: bf16 rows out, bf16 outputs back "
+                        "(device-side plan / pack / combine, no host synchronisation; the step replayed as one CUDA "
+                        "graph)", "flops_per_pass": flops}
 
 
 def stack_prefill_lines(dev, world, rank, steps, warmup, blocks=None, layers=LAYERS, tokens=8192):
     """BASELINE configs[4](b): 8 packed sequences of 1024 tokens (8192) through the 16-layer stack, one step = the
     whole prefill. One GPU: MoeBlock.prefill per layer (norm, router, expert sort, grouped GEMMs, finalize) on the
     decode stack's blocks. N ranks: expert parallel, strong scaling (8192 / N tokens per rank; every rank holds
-    the router, norm, shared expert and experts 0-7 of each layer and its round-robin share of the others)."""
+    the router, norm, shared expert and experts 0-7 of each layer and its share of the others, dealt as a snake).
+    The step is replayed as one CUDA graph."""
     from oracle import moe_oracle as O
     per_rank = tokens // world
     x = O.make_tokens(per_rank, seed=30 + rank).to(dev)
@@ -436,18 +454,35 @@ def stack_prefill_lines(dev, world, rank, steps, warmup, blocks=None, layers=LAY
             return h
     for _ in range(warmup):
         step()
+    torch.cuda.synchronize()
+    # the whole 16-layer step (with EP: its 32 NCCL all-to-alls too) in one CUDA graph: no host synchronisation
+    # anywhere in it, and every rank captures and replays the same collectives in the same order
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        step()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    for _ in range(warmup):
+        graph.replay()
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     s_ev, e_ev = torch.cuda.Event(True), torch.cuda.Event(True)
     s_ev.record()
     for _ in range(steps):
-        step()
+        graph.replay()
     e_ev.record()
     torch.cuda.synchronize()
     t = torch.tensor([s_ev.elapsed_time(e_ev) / steps], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.barrier()
+    del graph  # (a graph holding NCCL calls is released before the process group)
+    if world > 1:
         errs = {k: v for ep in eps_blocks for k, v in ep.errors().items()}
         if errs:
             raise RuntimeError(f"stack prefill EP device errors: {errs}")

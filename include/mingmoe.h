@@ -218,8 +218,10 @@ MV_API int mv_moe_prefill_f32(const mv_moe_weights* w, const void* x, long long 
  *                 zero tail only. Rows and metadata then cross in one all-to-all.
  *  mv_ep_unpack   ids / wts [world * cap, NK] of the received wire rows recv_rows [world * cap, H + 8]: column 0 =
  *                 (slot, weight) of a place in use, the rest -1 / 0.
- *  mv_ep_combine  out [N, H] bf16 = x + y_local + the returned fp32 outputs back[pos[n, k]] of n's remote pairs
- *                 (k order), rounded once. */
+ *  mv_ep_narrow   out[i] = bf16(y[i]) for n values (n % 8 == 0): the received rows' fp32 outputs (one weighted
+ *                 pair each) rounded once for the return exchange, halving its bytes.
+ *  mv_ep_combine  out [N, H] bf16 = x + y_local + the returned outputs back[pos[n, k]] of n's remote pairs
+ *                 (k order; back_dtype MV_F32 or MV_BF16, added in fp32), rounded once. */
 MV_API size_t mv_ep_workspace_bytes(void);
 MV_API int mv_ep_plan(const int* ids, const float* wts, int N, int NK, int K, const int* owner, const int* slot, int E,
                       int rank, int world, int cap, int* ids_local, float* wts_local, int* pos, int* send_src,
@@ -227,8 +229,9 @@ MV_API int mv_ep_plan(const int* ids, const float* wts, int N, int NK, int K, co
 MV_API int mv_ep_pack(const void* xn, long long x_stride, int H, const int* send_src, const int* send_meta, int world,
                       int cap, void* send_rows, void* stream);
 MV_API int mv_ep_unpack(const void* recv_rows, int H, int world, int cap, int NK, int* ids, float* wts, void* stream);
-MV_API int mv_ep_combine(const void* x, long long x_stride, const float* y_local, const float* back, const int* pos,
-                         int N, int K, int H, void* out, void* stream);
+MV_API int mv_ep_narrow(const float* y, long long n, void* out, void* stream);
+MV_API int mv_ep_combine(const void* x, long long x_stride, const float* y_local, const void* back, int back_dtype,
+                         const int* pos, int N, int K, int H, void* out, void* stream);
 
 /* Workspace for the fastest decode path (the tensor-core kernel, bf16 weights, H and I multiples of 128,
  * H <= 2048): larger than mv_moe_decode_workspace_bytes, which is the minimum (with the minimum the CUDA-core

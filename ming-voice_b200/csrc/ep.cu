@@ -178,9 +178,39 @@ __global__ void __launch_bounds__(256) unpack_kernel(const uint16_t* __restrict_
   }
 }
 
+// The remote rows' outputs to bf16 for the return exchange: out[i] = bf16(y[i]), 8 values per thread. A received
+// row carries exactly one pair, so this is that pair's weighted output rounded once -- the rounding the
+// reference's grouped GEMM applies to every pair's output (its bf16 output cache) -- and it halves the bytes
+// that cross NVLink on the way back.
+__global__ void __launch_bounds__(256) narrow_kernel(const float* __restrict__ y, long long n8,
+                                                     uint4* __restrict__ out) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(y)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(y)[2 * i + 1];
+    uint4 o;
+    o.x = static_cast<uint32_t>(f2bf(a.x)) | (static_cast<uint32_t>(f2bf(a.y)) << 16);
+    o.y = static_cast<uint32_t>(f2bf(a.z)) | (static_cast<uint32_t>(f2bf(a.w)) << 16);
+    o.z = static_cast<uint32_t>(f2bf(b.x)) | (static_cast<uint32_t>(f2bf(b.y)) << 16);
+    o.w = static_cast<uint32_t>(f2bf(b.z)) | (static_cast<uint32_t>(f2bf(b.w)) << 16);
+    out[i] = o;
+  }
+}
+
+// four returned values of row pq at column group c, as fp32 (fp32 or bf16 rows)
+template <bool B16>
+__device__ __forceinline__ float4 back4(const void* back, long long pq, int H, int c) {
+  if (B16) {
+    const uint2 v = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(back) + pq * H)[c];
+    return make_float4(bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y));
+  }
+  return reinterpret_cast<const float4*>(static_cast<const float*>(back) + pq * H)[c];
+}
+
 // out[n, 4c..4c+3] = bf16(x + y_local + the returned outputs of n's remote pairs in k order)
+template <bool B16>
 __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict__ x, long long x_stride,
-                                                      const float* __restrict__ y_local, const float* __restrict__ back,
+                                                      const float* __restrict__ y_local, const void* __restrict__ back,
                                                       const int* __restrict__ pos, int N, int K, int H,
                                                       uint16_t* __restrict__ out) {
   const int h4 = H / 4;
@@ -194,7 +224,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint16_t* __restrict
     for (int k = 0; k < K; ++k) {
       const int pq = pos[static_cast<long long>(n) * K + k];
       if (pq < 0) continue;
-      const float4 b = reinterpret_cast<const float4*>(back + static_cast<long long>(pq) * H)[c];
+      const float4 b = back4<B16>(back, pq, H, c);
       v0 += b.x;
       v1 += b.y;
       v2 += b.z;
@@ -269,16 +299,32 @@ extern "C" int mv_ep_unpack(const void* recv_rows, int H, int world, int cap, in
   return cuda_status(cudaGetLastError(), "mv_ep_unpack launch");
 }
 
-extern "C" int mv_ep_combine(const void* x, long long x_stride, const float* y_local, const float* back,
-                             const int* pos, int N, int K, int H, void* out, void* stream) {
+extern "C" int mv_ep_narrow(const float* y, long long n, void* out, void* stream) {
+  if (y == nullptr || out == nullptr) return fail(MV_ERR_INVALID, "mv_ep_narrow: null pointer argument");
+  if (n < 0 || n % 8 || !aligned16(y) || !aligned16(out)) return fail(MV_ERR_ALIGN, "mv_ep_narrow: 8k values, aligned");
+  if (n == 0) return MV_OK;
+  const long long n8 = n / 8;
+  const unsigned int blocks = static_cast<unsigned int>((n8 + 255) / 256 < 148 * 8 ? (n8 + 255) / 256 : 148 * 8);
+  ep::narrow_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, n8, static_cast<uint4*>(out));
+  return cuda_status(cudaGetLastError(), "mv_ep_narrow launch");
+}
+
+extern "C" int mv_ep_combine(const void* x, long long x_stride, const float* y_local, const void* back,
+                             int back_dtype, const int* pos, int N, int K, int H, void* out, void* stream) {
   if (x == nullptr || y_local == nullptr || back == nullptr || pos == nullptr || out == nullptr)
     return fail(MV_ERR_INVALID, "mv_ep_combine: null pointer argument");
+  if (back_dtype != MV_F32 && back_dtype != MV_BF16)
+    return fail(MV_ERR_UNSUPPORTED, "mv_ep_combine: returned outputs must be f32 or bf16");
   if (H % 4 || x_stride % 4 || !aligned16(y_local) || !aligned16(back))
     return fail(MV_ERR_ALIGN, "mv_ep_combine: aligned rows needed");
   if (N == 0) return MV_OK;
   const long long total = static_cast<long long>(N) * H / 4;
   const unsigned int blocks = static_cast<unsigned int>((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
-  ep::combine_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(x), x_stride, y_local, back, pos, N, K, H, static_cast<uint16_t*>(out));
+  if (back_dtype == MV_BF16)
+    ep::combine_kernel<true><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(x), x_stride, y_local, back, pos, N, K, H, static_cast<uint16_t*>(out));
+  else
+    ep::combine_kernel<false><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(x), x_stride, y_local, back, pos, N, K, H, static_cast<uint16_t*>(out));
   return cuda_status(cudaGetLastError(), "mv_ep_combine launch");
 }

@@ -75,7 +75,8 @@ _SIGS = {
     "mv_ep_plan": (I32, [P, P, I32, I32, I32, P, P, I32, I32, I32, I32, P, P, P, P, P, P, SZ, P]),
     "mv_ep_pack": (I32, [P, I64, I32, P, P, I32, I32, P, P]),
     "mv_ep_unpack": (I32, [P, I32, I32, I32, I32, P, P, P]),
-    "mv_ep_combine": (I32, [P, I64, P, P, P, I32, I32, I32, P, P]),
+    "mv_ep_narrow": (I32, [P, I64, P, P]),
+    "mv_ep_combine": (I32, [P, I64, P, P, I32, P, I32, I32, I32, P, P]),
 }
 
 _lib = None

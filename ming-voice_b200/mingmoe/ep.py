@@ -1,8 +1,9 @@
 """Expert-parallel (EP) prefill of one MoE block over a torch.distributed process group (NCCL, one rank per GPU).
 
 Placement. Every rank holds the router, the RMSNorm weight and the shared-expert slots (data parallel), the
-`replicated` experts (the hottest ones: their pairs never leave the rank), and a round-robin share of the
-other ("cold") experts: cold expert number c (in id order) lives on rank c % world. With BASELINE's Zipf router
+`replicated` experts (the hottest ones: their pairs never leave the rank), and a share of the other ("cold")
+experts dealt in id order as a snake (ranks 0..W-1, then W-1..0, ...), which spreads a popularity that falls with
+the expert id evenly over the ranks. With BASELINE's Zipf router
 bias six experts take ~80 % of all routed pairs, so sharding them would serialise the step on their owners;
 replicating them costs 17 MB per expert of the 180 GB on each GPU.
 
@@ -15,9 +16,10 @@ fixed capacity `cap` of pairs per peer, so the step can be captured in a CUDA gr
   3. one NCCL all-to-all of fixed size moves the wire rows (the one exchange step of the block);
   4. ONE tcgen05 grouped-GEMM pass (mv_moe_prefill_f32, fp32 outputs) over the own rows (local pairs; the rest -1,
      skipped by the expert sort) and the received rows where they landed (their one pair; unused places -1);
-     the received rows' outputs go back with a second all-to-all;
-  5. mv_ep_combine adds, per token, the residual, the local sum and its remote pairs' outputs in pair order,
-     rounding once to bf16 -- the same sum a single GPU makes.
+     the received rows' outputs go back with a second all-to-all, as bf16 (mv_ep_narrow: each is one weighted
+     pair's output, rounded once, which is where the reference's grouped GEMM rounds every pair's output too);
+  5. mv_ep_combine adds, per token in fp32, the residual, the local sum and its remote pairs' outputs in pair
+     order, rounding once to bf16.
 More than `cap` pairs for one peer is an error recorded in the plan's workspace (the excess pairs are dropped);
 `plan_capacity` measures what a batch needs. No kernel reads another GPU's memory: everything remote arrives
 through NCCL. With an `experts_fn` (the CPU tests) the same step runs on torch tensors with data-dependent
@@ -33,7 +35,9 @@ from . import moe
 
 def placement(E: int, world: int, replicated=()):
     """owner[e], slot[e] for every routed expert e: replicated experts -> slot i on every rank (owner -1 =
-    "this rank"); cold experts -> rank c % world, slot n_rep + c // world. Also each rank's stack order."""
+    "this rank"); the c-th cold expert -> slot n_rep + c // world on rank c % world in even rounds and
+    world - 1 - c % world in odd ones (a snake: with popularity falling with the expert id, as under the Zipf
+    router bias, no rank collects the most popular expert of every round). Also each rank's stack order."""
     rep = list(replicated)
     rset = set(rep)
     cold = [e for e in range(E) if e not in rset]
@@ -41,10 +45,15 @@ def placement(E: int, world: int, replicated=()):
     slot = [0] * E
     for i, e in enumerate(rep):
         slot[e] = i
+
+    def rank_of(c):
+        rnd, pos = divmod(c, world)
+        return pos if rnd % 2 == 0 else world - 1 - pos
+
     for c, e in enumerate(cold):
-        owner[e] = c % world
+        owner[e] = rank_of(c)
         slot[e] = len(rep) + c // world
-    stacks = [rep + [e for c, e in enumerate(cold) if c % world == r] for r in range(world)]
+    stacks = [rep + [e for c, e in enumerate(cold) if rank_of(c) == r] for r in range(world)]
     return owner, slot, stacks
 
 
@@ -130,7 +139,8 @@ class EPMoeBlock:
                 send_rows=torch.zeros(R, H + 8, dtype=torch.bfloat16, device=dev),  # wire rows: H values + tail
                 recv_rows=torch.zeros(R, H + 8, dtype=torch.bfloat16, device=dev),
                 y32=torch.empty(N + R, H, dtype=torch.float32, device=dev),
-                back=torch.empty(R, H, dtype=torch.float32, device=dev),
+                back_send=torch.empty(R, H, dtype=torch.bfloat16, device=dev),  # received rows' outputs, bf16
+                back=torch.empty(R, H, dtype=torch.bfloat16, device=dev),
                 out=torch.empty(N, H, dtype=torch.bfloat16, device=dev),
                 owner=self._owner_raw.to(dev),
                 slot=self.slot.to(torch.int32).to(dev),
@@ -181,10 +191,12 @@ class EPMoeBlock:
         L.check(lib.mv_moe_prefill_f32(C.byref(wst), L.ptr(xn), H, N, L.ptr(bf["recv_rows"]), H + 8, L.ptr(ids_all),
                                        L.MV_I32, L.ptr(wts_all), N + R, NK, None, 0, L.ptr(y32), 0, L.ptr(pws),
                                        pws.numel(), st), "mv_moe_prefill_f32")
-        dist.all_to_all_single(bf["back"], y32[N:], group=self.group)
+        # the received rows' outputs (one weighted pair each) go back as bf16: rounded once, half the bytes
+        L.check(lib.mv_ep_narrow(L.ptr(y32[N:]), R * H, L.ptr(bf["back_send"]), st), "mv_ep_narrow")
+        dist.all_to_all_single(bf["back"], bf["back_send"], group=self.group)
         out = bf["out"]
-        L.check(lib.mv_ep_combine(L.ptr(x), x.stride(0), L.ptr(y32), L.ptr(bf["back"]), L.ptr(bf["pos"]), N, K, H,
-                                  L.ptr(out), st), "mv_ep_combine")
+        L.check(lib.mv_ep_combine(L.ptr(x), x.stride(0), L.ptr(y32), L.ptr(bf["back"]), L.MV_BF16, L.ptr(bf["pos"]),
+                                  N, K, H, L.ptr(out), st), "mv_ep_combine")
         return out
 
     def errors(self):

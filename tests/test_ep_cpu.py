@@ -88,7 +88,7 @@ def test_placement_tables():
     sys.path.insert(0, __import__("os").path.join(__import__("os").path.dirname(__file__), "..", "ming-voice_b200"))
     from mingmoe.ep import placement
     owner, slot, stacks = placement(8, 3, replicated=(2, 5))
-    assert stacks == [[2, 5, 0, 4], [2, 5, 1, 6], [2, 5, 3, 7]]
+    assert stacks == [[2, 5, 0, 7], [2, 5, 1, 6], [2, 5, 3, 4]]  # snake: ranks 0 1 2, then 2 1 0
     for r, st in enumerate(stacks):
         for i, e in enumerate(st):
             assert slot[e] == i and owner[e] in (-1, r)
