@@ -148,7 +148,10 @@ class EPMoeBlock:
             self._bufs[key] = bf
         return bf
 
-    def _forward_cuda(self, x):
+    PHASES = ("norm+route", "plan+pack", "exchange out", "unpack", "grouped GEMM+narrow", "exchange back", "combine")
+
+    def _forward_cuda(self, x, events=None):
+        """The step; `events` (len(PHASES) + 1 CUDA events, or None) are recorded at the phase boundaries."""
         import ctypes as C
         import fused_ops
         from . import _lib as L
@@ -164,6 +167,8 @@ class EPMoeBlock:
         st = L.stream_ptr(dev)
         lib = L.lib()
         xn = bf["xn"]
+        mark = (lambda i: events[i].record()) if events is not None else (lambda i: None)
+        mark(0)
         if b.norm_w is not None:
             L.check(lib.mv_rmsnorm(L.ptr(x), L.MV_BF16, x.stride(0), L.ptr(b.norm_w), L.MV_BF16, L.ptr(xn), L.MV_BF16,
                                    N, H, C.c_float(b.eps), st), "mv_rmsnorm")
@@ -172,6 +177,7 @@ class EPMoeBlock:
         fused_ops.moe_route(xn, b.router_w, b.router_bias, b.n_group, b.topk_group, K, b.route_scale, bf["logits"],
                             bf["ids"], bf["wts"], mode=b.route_mode, n_shared=len(b.shared_ids),
                             shared_id=b.shared_ids[0] if b.shared_ids else b.E, w_scale=b.router_s)
+        mark(1)
         ws = L.workspace("ep", int(lib.mv_ep_workspace_bytes()), dev)
         ids_all, wts_all = bf["ids_all"], bf["wts_all"]
         L.check(lib.mv_ep_plan(L.ptr(bf["ids"]), L.ptr(bf["wts"]), N, NK, K, L.ptr(bf["owner"]), L.ptr(bf["slot"]),
@@ -179,10 +185,13 @@ class EPMoeBlock:
                                L.ptr(bf["send_src"]), L.ptr(bf["send_meta"]), L.ptr(ws), ws.numel(), st), "mv_ep_plan")
         L.check(lib.mv_ep_pack(L.ptr(xn), H, H, L.ptr(bf["send_src"]), L.ptr(bf["send_meta"]), W, cap,
                                L.ptr(bf["send_rows"]), st), "mv_ep_pack")
+        mark(2)
         # the exchange: rows and their (slot, weight) tails in one all-to-all
         dist.all_to_all_single(bf["recv_rows"], bf["send_rows"], group=self.group)
+        mark(3)
         L.check(lib.mv_ep_unpack(L.ptr(bf["recv_rows"]), H, W, cap, NK, L.ptr(ids_all[N:]), L.ptr(wts_all[N:]), st),
                 "mv_ep_unpack")
+        mark(4)
         # one grouped-GEMM pass: own rows from xn, received rows where they landed (wire row stride H + 8)
         wst = moe.weights_struct(b.w_gu, b.w_d, b.s_gu, b.s_d)
         nbytes = lib.mv_moe_prefill_workspace_bytes(N + R, NK, H, b.I, b.w_gu.shape[0], L.dt(b.w_gu))
@@ -193,11 +202,26 @@ class EPMoeBlock:
                                        pws.numel(), st), "mv_moe_prefill_f32")
         # the received rows' outputs (one weighted pair each) go back as bf16: rounded once, half the bytes
         L.check(lib.mv_ep_narrow(L.ptr(y32[N:]), R * H, L.ptr(bf["back_send"]), st), "mv_ep_narrow")
+        mark(5)
         dist.all_to_all_single(bf["back"], bf["back_send"], group=self.group)
+        mark(6)
         out = bf["out"]
         L.check(lib.mv_ep_combine(L.ptr(x), x.stride(0), L.ptr(y32), L.ptr(bf["back"]), L.MV_BF16, L.ptr(bf["pos"]),
                                   N, K, H, L.ptr(out), st), "mv_ep_combine")
+        mark(7)
         return out
+
+    def phase_times(self, x, reps=20, warmup=3):
+        """Device time of each phase of the step (PHASES, microseconds, mean over `reps` eager steps) on this rank,
+        from CUDA events at the phase boundaries; an exchange phase includes waiting for the slowest peer.
+        Host-synchronising: a measurement utility, not for the hot loop."""
+        for _ in range(warmup):
+            self._forward_cuda(x)
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(self.PHASES) + 1)] for _ in range(reps)]
+        for ev in evs:
+            self._forward_cuda(x, events=ev)
+        torch.cuda.synchronize(x.device)
+        return [sum(ev[i].elapsed_time(ev[i + 1]) for ev in evs) / reps * 1e3 for i in range(len(self.PHASES))]
 
     def errors(self):
         """Device-side errors of the plan (capacity exceeded: code 3, info = the peer); host-synchronising."""
