@@ -65,9 +65,10 @@ def peaks_tensor():
 
 
 def ncu_traffic():
-    """dram read+write bytes per launch of the decode kernel from the committed ncu summary (or None)."""
+    """dram read+write bytes per launch of the decode kernel (the one-token kernel at M=1) from the committed ncu
+    summary (or None)."""
     import re
-    path = os.path.join(ROOT, "profiles", "moe_decode_kernel_block_m1.md")
+    path = os.path.join(ROOT, "profiles", "decode_m1_kernel_block_m1.md")
     try:
         m = re.search(r"traffic_bytes_per_launch:\s*([0-9.e+]+)", open(path).read())
         return float(m.group(1)) if m else None
