@@ -47,6 +47,11 @@ constexpr int kGroups = 4;   // ring slots = consuming groups
 constexpr int kGW = 4;       // warps per group = K parts of a row
 constexpr int kWarps = kGroups * kGW;
 constexpr int kThreads = kWarps * 32;
+// Ring slot: 40 KB, not the general kernel's 32 KB. A gate/up stage still fills 32 KB of it (RG rows of gate and
+// of up), but a down stage takes 14 bf16 rows of 2816 bytes instead of 11, so a CTA's 112 (expert, row) entries
+// of the BASELINE block fit 8 stages = two rounds of the 4 groups after the grid barrier instead of three (the
+// shared memory has room: 217 KB of 227).
+constexpr int kSlotBytes = 40960;
 
 // Shared-memory layout (byte offsets), computed identically on the host (size check) and the device.
 struct Layout {
@@ -63,7 +68,7 @@ __host__ __device__ inline unsigned int take(unsigned int& o, unsigned int bytes
 
 __host__ __device__ inline Layout layout(int H, int I, int E, int u_max, int nhc, int gsc_cap, int RG, bool int8) {
   Layout L;
-  unsigned int o = kGroups * kStageBytes;  // the ring, at offset 0 (1024-byte aligned)
+  unsigned int o = kGroups * kSlotBytes;  // the ring, at offset 0 (1024-byte aligned)
   L.bars = take(o, kGroups * 8, 8);
   L.xn = take(o, H * 2, 16);
   L.abuf = take(o, u_max * I * 4, 16);
@@ -97,7 +102,7 @@ struct Stage {
 
 // Gate rows per stage: the largest power of two <= 8 with 2 RG rows (gate + up) in one stage.
 __host__ __device__ constexpr int rows_per_stage(int row_bytes) {
-  return 2 * 8 * row_bytes <= kStageBytes ? 8 : (2 * 4 * row_bytes <= kStageBytes ? 4 : (2 * 2 * row_bytes <= kStageBytes ? 2 : 1));
+  return 2 * 8 * row_bytes <= kSlotBytes ? 8 : (2 * 4 * row_bytes <= kSlotBytes ? 4 : (2 * 2 * row_bytes <= kSlotBytes ? 2 : 1));
 }
 
 // Specialised for the hidden size H and the expert width I (the model's, so every offset, trip count and bound
@@ -107,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
   using WT = W<INT8>;
   constexpr int VEC = WT::vec;
   constexpr int RG = rows_per_stage(H * WT::esz);
-  constexpr int DP0 = kStageBytes / (I * WT::esz);
+  constexpr int DP0 = kSlotBytes / (I * WT::esz);
   constexpr int DP = DP0 < kNhMax ? DP0 : kNhMax;  // down rows per stage
   constexpr int nvh = H / VEC, nqh = nvh / kGW;    // 16-byte chunks of a gate/up row; of its K quarter
   constexpr int nvi = I / VEC, nqi = nvi / kGW;    // ... of a down row
@@ -157,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
   const uint32_t drow_b = static_cast<uint32_t>(I) * WT::esz;
   const uint64_t pol = policy_evict_first();
   const bool issuer = kq == 0 && lane == 0;  // issues the copies of the group's slot
-  uint8_t* slot = ring + static_cast<size_t>(grp) * kStageBytes;
+  uint8_t* slot = ring + static_cast<size_t>(grp) * kSlotBytes;
   uint64_t* full = bars + grp;
   uint32_t ph = 0;    // parity of the slot's next fill
   int gcount = 0;     // gate/up stages consumed by the group (double-buffered partial sums)
