@@ -1,6 +1,6 @@
 // Expert-parallel prefill: the device side of one rank's dispatch and combine (the exchange itself is two NCCL
-// all-to-alls of fixed size issued by the host, rows out and fp32 outputs back; nothing here synchronises the
-// host).
+// all-to-alls of fixed size issued by the host, wire rows out and bf16 outputs back; nothing here synchronises
+// the host).
 //
 // Placement (ming-voice is single-GPU, engine.py:34; expert parallelism is new): every rank holds the router,
 // the norm, the shared-expert slots and the replicated hot experts; each other ("cold") expert lives on one rank.
@@ -17,8 +17,9 @@
 //                   bf16 values and a 16-byte tail (slot, weight, in-use flag), so rows and their metadata cross
 //                   in ONE all-to-all; a place past the count gets only its tail (flag 0).
 //   mv_ep_unpack    received tails -> ids / weights of the received rows (id -1 for unused places).
+//   mv_ep_narrow    the received rows' fp32 outputs (one weighted pair each) to bf16 for the return exchange.
 //   mv_ep_combine   out[n] = bf16(x[n] + y_local[n] + sum over n's remote pairs, in k order, of their returned
-//                   fp32 outputs): one rounding, the same sum as one GPU computes.
+//                   outputs), added in fp32 and rounded once.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -30,9 +31,10 @@ namespace ep {
 constexpr int kMaxWorld = 8;
 constexpr int kPlanThreads = 1024;
 
-// STAGED: the routed ids and the owner table are first copied into shared memory (coalesced), so the two
-// per-thread passes over contiguous pair ranges (which keep the token order) read shared memory, not scattered
-// global words.
+// STAGED: the routed ids and weights, the owner table and the slot table are first copied into shared memory
+// (coalesced, 8 loads in flight per thread), so the two per-thread passes over contiguous pair ranges (which keep
+// the token order) read shared memory only; unstaged, every pair costs dependent global loads in the pass loops
+// (the one-CTA plan took ~45 us for 12 K pairs that way).
 template <bool STAGED>
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restrict__ ids, const float* __restrict__ wts,
                                                             int N, int NK, int K, const int* __restrict__ owner,
@@ -43,20 +45,46 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
                                                             WsHeader* ws) {
   __shared__ int s_warp[kPlanThreads / 32][kMaxWorld];
   __shared__ int s_base[kMaxWorld];
-  extern __shared__ int s_dyn[];  // STAGED: [E] owner, [N * K] routed ids
+  extern __shared__ int s_dyn[];  // STAGED: [E] owner, [E] slot, [N * K] routed ids, [N * K] routed weights
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const long long P = static_cast<long long>(N) * K;
   const long long chunk = (P + kPlanThreads - 1) / kPlanThreads;
   const long long p0 = chunk * t, p1 = min(P, p0 + chunk);
   int* s_owner = s_dyn;
-  int* s_ids = s_dyn + E;
+  int* s_slot = s_dyn + E;
+  int* s_ids = s_dyn + 2 * E;
+  float* s_wts = reinterpret_cast<float*>(s_dyn + 2 * E + P);
   if (STAGED) {
-    for (int e = t; e < E; e += kPlanThreads) s_owner[e] = owner[e];
-    for (long long q = t; q < P; q += kPlanThreads) s_ids[q] = ids[(q / K) * NK + q % K];
+    for (int e = t; e < E; e += kPlanThreads) {
+      s_owner[e] = owner[e];
+      s_slot[e] = slot[e];
+    }
+    constexpr int kB = 8;  // loads in flight per thread
+    for (long long q0 = t; q0 < P; q0 += kB * kPlanThreads) {
+      int iv[kB];
+      float wv[kB];
+#pragma unroll
+      for (int u = 0; u < kB; ++u) {
+        const long long q = q0 + static_cast<long long>(u) * kPlanThreads;
+        const long long iq = (q / K) * NK + q % K;
+        iv[u] = q < P ? ids[iq] : 0;
+        wv[u] = q < P ? wts[iq] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kB; ++u) {
+        const long long q = q0 + static_cast<long long>(u) * kPlanThreads;
+        if (q < P) {
+          s_ids[q] = iv[u];
+          s_wts[q] = wv[u];
+        }
+      }
+    }
     __syncthreads();
   }
   auto id_at = [&](long long q) { return STAGED ? s_ids[q] : ids[(q / K) * NK + q % K]; };
+  auto wt_at = [&](long long q, long long iq) { return STAGED ? s_wts[q] : wts[iq]; };
   auto owner_of = [&](int e) { return STAGED ? s_owner[e] : owner[e]; };
+  auto slot_of = [&](int e) { return STAGED ? s_slot[e] : slot[e]; };
   // pass 1: this thread's pairs per owner
   int cnt[kMaxWorld];
 #pragma unroll
@@ -115,8 +143,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
         if (dd == d) j = off[dd]++;
       if (j < cap) {
         send_src[d * cap + j] = n;
-        send_meta[(static_cast<long long>(d) * (cap + 1) + j) * 2] = slot[e];
-        send_meta[(static_cast<long long>(d) * (cap + 1) + j) * 2 + 1] = __float_as_int(wts[iq]);
+        send_meta[(static_cast<long long>(d) * (cap + 1) + j) * 2] = slot_of(e);
+        send_meta[(static_cast<long long>(d) * (cap + 1) + j) * 2 + 1] = __float_as_int(wt_at(q, iq));
         pq = d * cap + j;
       } else {
         raise_error(ws, kErrOverflow, static_cast<unsigned int>(d));
@@ -124,8 +152,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
       ids_local[iq] = -1;
       wts_local[iq] = 0.f;
     } else {
-      ids_local[iq] = (e >= 0 && e < E) ? slot[e] : -1;
-      wts_local[iq] = wts[iq];
+      ids_local[iq] = (e >= 0 && e < E) ? slot_of(e) : -1;
+      wts_local[iq] = wt_at(q, iq);
     }
     pos[static_cast<long long>(n) * K + k] = pq;
   }
@@ -255,9 +283,9 @@ extern "C" int mv_ep_plan(const int* ids, const float* wts, int N, int NK, int K
   if (N < 0 || K < 1 || NK < K || E < 1 || cap < 1) return fail(MV_ERR_INVALID, "mv_ep_plan: bad shape");
   if (workspace == nullptr || workspace_bytes < kWsHeaderBytes)
     return fail(MV_ERR_WORKSPACE, "mv_ep_plan: workspace of %zu bytes needed", kWsHeaderBytes);
-  const size_t dyn = (static_cast<size_t>(E) + static_cast<size_t>(N) * K) * sizeof(int);
+  const size_t dyn = (2 * static_cast<size_t>(E) + 2 * static_cast<size_t>(N) * K) * sizeof(int);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dyn <= 200 * 1024) {  // ids and owner table staged in shared memory
+  if (dyn <= 200 * 1024) {  // ids, weights, owner and slot tables staged in shared memory
     cudaError_t e = cudaFuncSetAttribute(ep::plan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(dyn));
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(ep plan)");
