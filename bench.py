@@ -398,7 +398,7 @@ def ep_prefill_lines(dev, world, rank, steps, warmup):
     errs = ep.errors()
     if errs:
         raise RuntimeError(f"EP prefill device errors: {errs}")
-    # per-phase device times (eager steps, CUDA events at the phase boundaries), max over ranks
+    # per-phase device times (graph replays, event nodes at the phase boundaries), max over ranks
     ph = torch.tensor(ep.phase_times(x), dtype=torch.float64, device=dev)
     torch.distributed.all_reduce(ph, op=torch.distributed.ReduceOp.MAX)
     phases = {n: round(v, 1) for n, v in zip(ep.PHASES, ph.tolist())}
@@ -409,8 +409,8 @@ def ep_prefill_lines(dev, world, rank, steps, warmup):
             "exchange": f"NCCL all-to-all of fixed capacity {cap} pairs per peer: bf16 rows out, bf16 outputs back "
                         "(device-side plan / pack / combine, no host synchronisation; the step replayed as one CUDA "
                         "graph)", "flops_per_pass": flops,
-            "phases_us": {**phases, "note": "eager steps, CUDA events at the phase boundaries, each phase's max over "
-                                            "ranks (an exchange phase includes waiting for the slowest peer)"}}
+            "phases_us": {**phases, "note": "graph replays with event nodes at the phase boundaries, each phase's max "
+                                            "over ranks (an exchange phase includes waiting for the slowest peer)"}}
 
 
 def stack_prefill_lines(dev, world, rank, steps, warmup, blocks=None, layers=LAYERS, tokens=8192):

@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
                                                             WsHeader* ws) {
   __shared__ int s_warp[kPlanThreads / 32][kMaxWorld];
   __shared__ int s_base[kMaxWorld];
-  extern __shared__ int s_dyn[];  // STAGED: [E] owner, [E] slot, [N * K] routed ids, [N * K] routed weights
+  extern __shared__ int s_dyn[];  // STAGED: [E] owner, [E] slot, [N * K] routed ids, [N * K] weights, [N * K] pos
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const long long P = static_cast<long long>(N) * K;
   const long long chunk = (P + kPlanThreads - 1) / kPlanThreads;
@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
   int* s_slot = s_dyn + E;
   int* s_ids = s_dyn + 2 * E;
   float* s_wts = reinterpret_cast<float*>(s_dyn + 2 * E + P);
+  int* s_pos = s_dyn + 2 * E + 2 * P;
   if (STAGED) {
     for (int e = t; e < E; e += kPlanThreads) {
       s_owner[e] = owner[e];
@@ -149,13 +150,38 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int* __restric
       } else {
         raise_error(ws, kErrOverflow, static_cast<unsigned int>(d));
       }
-      ids_local[iq] = -1;
-      wts_local[iq] = 0.f;
+      if (STAGED) {  // in place: this thread has read pair q; the staged arrays are copied out below
+        s_ids[q] = -1;
+        s_wts[q] = 0.f;
+      } else {
+        ids_local[iq] = -1;
+        wts_local[iq] = 0.f;
+      }
     } else {
-      ids_local[iq] = (e >= 0 && e < E) ? slot_of(e) : -1;
-      wts_local[iq] = wt_at(q, iq);
+      const int il = (e >= 0 && e < E) ? slot_of(e) : -1;
+      const float wl = wt_at(q, iq);
+      if (STAGED) {
+        s_ids[q] = il;
+        s_wts[q] = wl;
+      } else {
+        ids_local[iq] = il;
+        wts_local[iq] = wl;
+      }
     }
-    pos[static_cast<long long>(n) * K + k] = pq;
+    if (STAGED)
+      s_pos[q] = pq;
+    else
+      pos[static_cast<long long>(n) * K + k] = pq;
+  }
+  if (STAGED) {  // the local ids / weights and the places, copied out coalesced (a thread's pairs are contiguous,
+                 // so stores straight from the pass above would touch a different line per lane)
+    __syncthreads();
+    for (long long q = t; q < P; q += kPlanThreads) {
+      const long long iq = (q / K) * NK + q % K;
+      ids_local[iq] = s_ids[q];
+      wts_local[iq] = s_wts[q];
+      pos[q] = s_pos[q];
+    }
   }
   // the shared-expert columns (k >= K) keep their (local) ids and weights
   for (long long q = t; q < static_cast<long long>(N) * (NK - K); q += kPlanThreads) {
@@ -283,9 +309,9 @@ extern "C" int mv_ep_plan(const int* ids, const float* wts, int N, int NK, int K
   if (N < 0 || K < 1 || NK < K || E < 1 || cap < 1) return fail(MV_ERR_INVALID, "mv_ep_plan: bad shape");
   if (workspace == nullptr || workspace_bytes < kWsHeaderBytes)
     return fail(MV_ERR_WORKSPACE, "mv_ep_plan: workspace of %zu bytes needed", kWsHeaderBytes);
-  const size_t dyn = (2 * static_cast<size_t>(E) + 2 * static_cast<size_t>(N) * K) * sizeof(int);
+  const size_t dyn = (2 * static_cast<size_t>(E) + 3 * static_cast<size_t>(N) * K) * sizeof(int);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dyn <= 200 * 1024) {  // ids, weights, owner and slot tables staged in shared memory
+  if (dyn <= 200 * 1024) {  // ids, weights, places, owner and slot tables staged in shared memory
     cudaError_t e = cudaFuncSetAttribute(ep::plan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(dyn));
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(ep plan)");

@@ -212,16 +212,33 @@ class EPMoeBlock:
         return out
 
     def phase_times(self, x, reps=20, warmup=3):
-        """Device time of each phase of the step (PHASES, microseconds, mean over `reps` eager steps) on this rank,
-        from CUDA events at the phase boundaries; an exchange phase includes waiting for the slowest peer.
+        """Device time of each phase of the step (PHASES, microseconds, mean over `reps` replays) on this rank. The
+        step is captured in a CUDA graph with event-record nodes at the phase boundaries (as the timed step runs,
+        so no host launch gaps count), replayed `reps` times. An exchange phase includes waiting for the slowest
+        peer. Every rank must call it with the same arguments (the graph holds the NCCL all-to-alls).
         Host-synchronising: a measurement utility, not for the hot loop."""
+        dev = x.device
         for _ in range(warmup):
             self._forward_cuda(x)
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(self.PHASES) + 1)] for _ in range(reps)]
-        for ev in evs:
-            self._forward_cuda(x, events=ev)
-        torch.cuda.synchronize(x.device)
-        return [sum(ev[i].elapsed_time(ev[i + 1]) for ev in evs) / reps * 1e3 for i in range(len(self.PHASES))]
+        evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(self.PHASES) + 1)]
+        torch.cuda.synchronize(dev)
+        stream = torch.cuda.Stream(device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            self._forward_cuda(x, events=evs)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                self._forward_cuda(x, events=evs)
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        tot = [0.0] * len(self.PHASES)
+        for _ in range(reps):
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            for i in range(len(self.PHASES)):
+                tot[i] += evs[i].elapsed_time(evs[i + 1])
+        del graph
+        return [v / reps * 1e3 for v in tot]
 
     def errors(self):
         """Device-side errors of the plan (capacity exceeded: code 3, info = the peer); host-synchronising."""
