@@ -635,6 +635,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
       }
     }
     named_bar(3 + grp, kGW * 32);  // the slot is read
+#ifdef MV_TRACE
+    if (tid == 0 && tk <= 2) MV_TRACE_AT(p, 17 + tk);  // group 0's first / second down stage consumed
+#endif
     Stage nxt{};
     const bool hn = next_owned(nxt);
     if (issuer && hn && ok) issue(nxt);
