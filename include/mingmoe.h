@@ -287,8 +287,9 @@ MV_API int mv_mask_pad_rows(void* ids, int ids_dtype, int N, int NK, const int* 
  * The scratch is a static 1 MiB device array per device; the first call on a device (with it current)
  * looks its address up, so make that call before any stream capture. Calls whose scratch need
  * (mv_block_decode_workspace_bytes) exceeds 1 MiB are rejected with MV_ERR_WORKSPACE. Every call runs the
- * CUDA-core decode kernel: the tensor-core kernel's layout (3.4 MB at M = 1 up to 50 MB at M = 16 for H=2048,
- * I=1408, 64 + 2 slots) does not fit the static scratch. Each call clears the
+ * CUDA-core decode kernels (the one-token kernel, once per token where mv_block_decode would, or the general
+ * one): the tensor-core kernel's layout (3.4 MB at M = 1 up to 50 MB at M = 16 for H=2048, I=1408, 64 + 2
+ * slots) does not fit the static scratch. Each call clears the
  * scratch's 256-byte header (barrier counters, error word) on `stream` before its launch.
  * status_out (device or pinned host memory, 2 x u32, may be NULL) receives the call's device-side error
  * code and location, as mv_workspace_status reports them. One scratch per device: calls that can run

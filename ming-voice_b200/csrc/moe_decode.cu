@@ -886,6 +886,33 @@ int decode_run(Params& p, const mv_moe_weights* w, void* workspace, size_t works
 #ifdef MV_TRACE
   p.trace = static_cast<unsigned long long*>(g_decode_trace);
 #endif
+  {  // several tokens with the router fused: the one-token kernel once per token (the block is per-token work). In
+    // the 16-layer graph: bf16 M = 2 2 x 36.6 vs 80.9 us per block for the tensor-core kernel (which wins from
+    // M = 3); int8 every M, since the general kernel dequantises every weight once per token on the CUDA cores
+    // (M = 16: 849 us per block, against 16 x 36.6 here)
+    const char* path = getenv("MINGMOE_DECODE_PATH");
+    if (M >= 2 && (M == 2 || int8) && p.router && (path == nullptr || path[0] == 'm')) {
+      decode::Params q = p;
+      q.M = 1;
+      const size_t lg1 = (static_cast<size_t>(p.E) * 4 + 255) & ~size_t(255);
+      q.logits_ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes);
+      q.a_g = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes + lg1);
+      const int id_bytes = p.ids_out_i64 ? 8 : 4;
+      int rc = kDecodeM1Unsuitable;
+      for (int t = 0; t < M; ++t) {
+        q.x = p.x + t * p.x_stride;
+        q.residual = p.residual != nullptr ? p.residual + static_cast<long long>(t) * H : nullptr;
+        q.out = p.out + static_cast<long long>(t) * H;
+        q.ids_out = p.ids_out != nullptr ? static_cast<uint8_t*>(p.ids_out) + static_cast<long long>(t) * nk_pairs * id_bytes
+                                         : nullptr;
+        q.wts_out = p.wts_out != nullptr ? p.wts_out + static_cast<long long>(t) * nk_pairs : nullptr;
+        q.logits_out = p.logits_out != nullptr ? p.logits_out + static_cast<long long>(t) * p.E : nullptr;
+        rc = decode_m1_run(q, int8, st);
+        if (rc != MV_OK) break;
+      }
+      if (rc != kDecodeM1Unsuitable) return rc;
+    }
+  }
   if (!int8) {  // the tensor-core kernel when the shapes and the workspace suit it (M >= kTcMinM)
     const char* path = getenv("MINGMOE_DECODE_PATH");
     const bool force_tc = path != nullptr && path[0] == 't';
