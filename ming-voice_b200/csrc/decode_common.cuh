@@ -223,6 +223,25 @@ __device__ __forceinline__ void chunk_fma(float& a0, float& a1, const uint4& wv,
   }
 }
 
+// The same without the scale: a0 / a1 += float(q) * x (int8, exact products of integers and the fp32 x before
+// the fp32 adds) or w * x (bf16). The caller multiplies the row's sum by its scale once.
+template <bool INT8>
+__device__ __forceinline__ void chunk_fma_unscaled(float& a0, float& a1, const uint4& wv, const float* xv) {
+  const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+  if (INT8) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float f0, f1, f2, f3;
+      i8x4_to_f32(w[q], f0, f1, f2, f3);
+      ffma2(a0, a1, f0, f1, xv[4 * q], xv[4 * q + 1]);
+      ffma2(a0, a1, f2, f3, xv[4 * q + 2], xv[4 * q + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ffma2(a0, a1, bf16lo(w[q]), bf16hi(w[q]), xv[2 * q], xv[2 * q + 1]);
+  }
+}
+
 __device__ __forceinline__ float ldscale(const void* base, long long idx, int bf16) {
   if (bf16) return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(base)[idx]) << 16);
   return reinterpret_cast<const float*>(base)[idx];

@@ -31,8 +31,10 @@
 //    (43.6 us) they delay the routed gate/up stream, issued at the end of the gate/up phase (42.1 us) they
 //    delay the slowest CTAs on the grid barrier, and neither shortened the down phase.
 //
-// Numerics: as moe_decode.cu (fp32 accumulation and intermediates; int8 dequantised element by element as
-// float(q) * float(scale), torch's dequantisation; RMSNorm as mv_rmsnorm).
+// Numerics: as moe_decode.cu (fp32 accumulation and intermediates; RMSNorm as mv_rmsnorm), except that an int8
+// row's products are float(q) * x and the row's partial sums are multiplied by its scale once (the dequantised
+// weight float(q) * float(scale) is never formed: one multiply per row instead of one per weight, ~17 % of the
+// consumers' instructions, which bound the int8 kernel; the difference is fp32 rounding, ~1e-7 relative).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -356,12 +358,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
           for (int r = 0; r < 8; ++r) {
             const int row = (r < 4 ? 0 : RG) + h * 4 + (r & 3);
             const uint4 wv = *reinterpret_cast<const uint4*>(slot + row * (H * WT::esz) + cofs[j]);
-            chunk_fma<INT8>(acc[r][0], acc[r][1], wv, xv[j], sc[r]);
+            chunk_fma_unscaled<INT8>(acc[r][0], acc[r][1], wv, xv[j]);
           }
         }
         float v[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = acc[r][0] + acc[r][1];
+        for (int r = 0; r < 8; ++r) v[r] = INT8 ? (acc[r][0] + acc[r][1]) * sc[r] : acc[r][0] + acc[r][1];
         reduce8(v);
         if ((lane & 3) == 0) {
           const int r = lane >> 2;  // 0..3: gate rows of the batch, 4..7: up rows
@@ -618,12 +620,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
 #pragma unroll
           for (int r = 0; r < 8; ++r) {
             const uint4 wv = *reinterpret_cast<const uint4*>(rows + r * (I * WT::esz) + dofs[j]);
-            chunk_fma<INT8>(acc[r][0], acc[r][1], wv, av[j], sc[r]);
+            chunk_fma_unscaled<INT8>(acc[r][0], acc[r][1], wv, av[j]);
           }
         }
         float v[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = acc[r][0] + acc[r][1];
+        for (int r = 0; r < 8; ++r) v[r] = INT8 ? (acc[r][0] + acc[r][1]) * sc[r] : acc[r][0] + acc[r][1];
         reduce8(v);
         if ((lane & 3) == 0 && (lane >> 2) < run) ypart[(u * nhc + r0 + (lane >> 2)) * kGW + kq] = v[0];
         k += run;
