@@ -167,6 +167,29 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
+// d{0,1} = a{0,1} + b (packed, each lane correctly rounded: the same value as __fadd_rn)
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+
+// Four signed int8 lanes of a 32-bit word -> exact fp32 values as i8x4_to_f32 does (the bytes placed in the low
+// mantissa byte of 2^23 by byte permutes), with the bias removed by two packed adds instead of four.
+__device__ __forceinline__ void i8x4_to_f32_packed(uint32_t w, float& f0, float& f1, float& f2, float& f3) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t hi = 0x4B000000u;
+  uint32_t b0, b1, b2, b3;
+  asm("prmt.b32 %0, %1, %2, 0x7540;" : "=r"(b0) : "r"(u), "r"(hi));
+  asm("prmt.b32 %0, %1, %2, 0x7541;" : "=r"(b1) : "r"(u), "r"(hi));
+  asm("prmt.b32 %0, %1, %2, 0x7542;" : "=r"(b2) : "r"(u), "r"(hi));
+  asm("prmt.b32 %0, %1, %2, 0x7543;" : "=r"(b3) : "r"(u), "r"(hi));
+  const float nbias = -8388736.0f;  // -(2^23 + 128): exact sums
+  fadd2(f0, f1, __uint_as_float(b0), __uint_as_float(b1), nbias);
+  fadd2(f2, f3, __uint_as_float(b2), __uint_as_float(b3), nbias);
+}
+
 // d{0,1} = a{0,1} * s (packed, each lane correctly rounded: the same value as __fmul_rn)
 __device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, float s) {
   asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"

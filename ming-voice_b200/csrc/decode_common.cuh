@@ -211,7 +211,7 @@ __device__ __forceinline__ void chunk_fma(float& a0, float& a1, const uint4& wv,
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       float f0, f1, f2, f3;
-      i8x4_to_f32(w[q], f0, f1, f2, f3);
+      i8x4_to_f32_packed(w[q], f0, f1, f2, f3);
       fmul2(f0, f1, f0, f1, sc);
       fmul2(f2, f3, f2, f3, sc);
       ffma2(a0, a1, f0, f1, xv[4 * q], xv[4 * q + 1]);
@@ -232,7 +232,7 @@ __device__ __forceinline__ void chunk_fma_unscaled(float& a0, float& a1, const u
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       float f0, f1, f2, f3;
-      i8x4_to_f32(w[q], f0, f1, f2, f3);
+      i8x4_to_f32_packed(w[q], f0, f1, f2, f3);
       ffma2(a0, a1, f0, f1, xv[4 * q], xv[4 * q + 1]);
       ffma2(a0, a1, f2, f3, xv[4 * q + 2], xv[4 * q + 3]);
     }
