@@ -20,8 +20,8 @@
 //    a = wts * silu(gate . xn) * (up . xn) in fp32, stored to the workspace. One grid barrier. Down: each CTA
 //    owns output rows [hd0, hd1) of every selected expert; y = sum_e w_d[e][h] . a_e, + residual, bf16.
 //  * Routing: the shared-expert (static) rows need no routing, so the first ring-full of them is copied at
-//    kernel entry and consumed while the router runs: warp w of CTA b computes the logit of expert w * G + b
-//    (fp64 dot, rounded once to fp32), a grid barrier publishes them, and every CTA makes the same selection
+//    kernel entry and consumed while the router runs: warps 4q..4q+3 of CTA b compute the K quarters of the
+//    logit of expert q * G + b (fp64 dots, added in order and rounded once to fp32), a grid barrier publishes them, and every CTA makes the same selection
 //    with all its threads (route::select_parallel: every expert's rank among the biased scores, ties to the
 //    lower id, so no serial rounds of arg-max; the router bias was staged in shared memory at entry) and writes
 //    its one-token expert table directly (static slots, then the picks in id order). The selection sits on the
@@ -242,11 +242,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
     if (b0 < p.nx_rw_bytes) bulk_prefetch_l2(p.nx_rw + b0, static_cast<uint32_t>(min(per, p.nx_rw_bytes - b0)));
     if (blockIdx.x == G - 1 && p.nx_norm != nullptr) bulk_prefetch_l2(p.nx_norm, static_cast<uint32_t>(H) * 2u);
   }
-  const int e_logit = warp * G + static_cast<int>(blockIdx.x);  // the expert whose logit this warp computes
+  // the logit this warp helps with: expert (warp / 4) * G + b, K quarter warp % 4 (4 warps per logit: a quarter
+  // of the dot each, so the logits are published ~4x sooner than with one warp per expert)
+  const int e_logit = (warp >> 2) * G + static_cast<int>(blockIdx.x);
+  const int lq = warp & 3;
+  constexpr int HQ = H / 4;
   const int resz = p.rw_dtype == MV_F32 ? 4 : (p.rw_dtype == MV_BF16 ? 2 : 1);
   if (lane == 0 && e_logit < p.E)
-    bulk_prefetch_l2(static_cast<const uint8_t*>(p.rw) + static_cast<size_t>(e_logit) * H * resz,
-                     static_cast<uint32_t>(H * resz));
+    bulk_prefetch_l2(static_cast<const uint8_t*>(p.rw) + (static_cast<size_t>(e_logit) * H + lq * HQ) * resz,
+                     static_cast<uint32_t>(HQ * resz));
   // the router bias into shared memory now: the selection reads it on the critical path, long after this load
   if (p.rbias != nullptr)
     for (int j = tid; j < p.E; j += kThreads) sbias[j] = p.rbias[j];
@@ -389,19 +393,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
     }
   };
 
-  // ---- router logits: warp w of CTA b computes expert w * G + b
+  // ---- router logits: warps 4q..4q+3 of CTA b compute the K quarters of expert q * G + b (fp64), thread 0 adds
+  // the quarters in order, rounds once to fp32 and publishes
   unsigned long long tgt1 = 0;
   if (e_logit < p.E) {
     double acc[1] = {0.0};
     const float rsc = p.rw_dtype == MV_I8 ? ldscale(p.rw_scale, e_logit, p.rw_scale_bf16) : 1.0f;
-    route::router_dot<1>(static_cast<const uint8_t*>(p.rw) + static_cast<size_t>(e_logit) * H * resz, p.rw_dtype, rsc,
-                         xn, H, 1, acc);
+    route::router_dot<1>(static_cast<const uint8_t*>(p.rw) + (static_cast<size_t>(e_logit) * H + lq * HQ) * resz,
+                         p.rw_dtype, rsc, xn + lq * HQ, HQ, 1, acc);
     const double v = warp_sum_d(acc[0]);
-    if (lane == 0) p.logits_ws[e_logit] = static_cast<float>(v);
+    if (lane == 0) red[warp] = v;
   }
   named_bar(1, kThreads);
-  if (tid == 0) MV_TRACE_AT(p, 2);
-  if (tid == 0) tgt1 = grid_arrive_gen(&p.ws->gen1, G);  // (fence + arrive by one thread after the CTA barrier)
+  if (tid == 0) {
+    for (int q = 0; q < kWarps / 4; ++q) {
+      const int e = q * G + static_cast<int>(blockIdx.x);
+      if (e < p.E) p.logits_ws[e] = static_cast<float>(((red[4 * q] + red[4 * q + 1]) + red[4 * q + 2]) + red[4 * q + 3]);
+    }
+    MV_TRACE_AT(p, 2);
+    tgt1 = grid_arrive_gen(&p.ws->gen1, G);  // (fence + arrive by the thread that wrote this CTA's logits)
+  }
 
   // ---- the first static stage of each group while the other CTAs' logits arrive
   if (grp < n_early) {
@@ -425,8 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
                            sel_gs, pr_e, pr_w);
   }
   if (tid == 0) MV_TRACE_AT(p, 15);
-  if (warp == 0) {
-    if (blockIdx.x == 0) {  // router outputs: ids / weights with the static slots appended, logits
+  if (warp == 1 && blockIdx.x == 0) {  // router outputs (beside warp 0's table): ids / weights, static slots, logits
+    {
       const int NKT = p.top_k + n_static;
       for (int k = lane; k < NKT; k += 32) {
         const long long id = k < p.top_k ? pr_e[k] : static_cast<long long>(p.static_id + k - p.top_k);
@@ -441,7 +452,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_m1_kernel(const Params p) 
       if (p.logits_out)
         for (int j = lane; j < p.E; j += 32) p.logits_out[j] = ld_cg_f32(p.logits_ws + j);
     }
-    if (tid == 0) MV_TRACE_AT(p, 16);
+  }
+  if (warp == 0) {
     {  // the expert table of one token: the static slots, then the valid picks (distinct experts) in id order
       const int K = p.top_k;
       const int pe = lane < K ? pr_e[lane] : -1;
@@ -679,7 +691,7 @@ int decode_m1_run(decode::Params& p, bool int8, cudaStream_t st) {
     kern = int8 ? decode_m1_kernel<true, 1536, 512> : decode_m1_kernel<false, 1536, 512>;
   if (kern == nullptr) return kDecodeM1Unsuitable;
   const int G = num_sms();
-  if (p.E > kWarps * G || p.E > 128 || p.top_k > 32 || p.top_k > p.E) return kDecodeM1Unsuitable;
+  if (p.E > (kWarps / 4) * G || p.E > 128 || p.top_k > 32 || p.top_k > p.E) return kDecodeM1Unsuitable;
   const int RG = rows_per_stage(H * esz);
   p.RG = RG;
   p.u_max = p.n_static + (p.top_k < p.E ? p.top_k : p.E);
