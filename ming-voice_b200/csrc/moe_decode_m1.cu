@@ -5,9 +5,9 @@
 //
 // The step streams ~U x 17 MB of expert weights (bf16, H=2048, I=1408) and little else; what limits a
 // weight-streaming kernel at this size is how many bytes each SM keeps in flight, and how fast its warps turn a
-// landed 32 KB stage into a free slot. The design:
+// landed stage into a free slot. The design:
 //
-//  * 16 warps = 4 groups of 4 warps, one 32 KB ring slot per group. There is no producer warp: the first warp of a
+//  * 16 warps = 4 groups of 4 warps, one 40 KB ring slot per group (kSlotBytes). There is no producer warp: the first warp of a
 //    group issues the bulk copies (TMA engine, evict-first) of the group's next stage into its own slot right
 //    after the group has finished reading it, so a slot never waits for another warp's turn, and without a
 //    producer warp the kernel runs 16 warps, i.e. up to 128 registers a thread.
