@@ -262,9 +262,11 @@ typedef struct mv_block {
                                   so the next block's routing starts from L2 (a layer stack links block l to l+1). */
 } mv_block;
 
-/* Decode step of one block for M <= 16 tokens in ONE cooperative kernel: replaces the patched single-token
- * MoE forward (engine.py:371-386: fused_ops.moe_route followed by fused_moe.fused_moe_decode), including the
- * RMSNorm before it (engine.py:229) and the decoder layer's residual. x [M, H] bf16 contiguous, out [M, H] bf16.
+/* Decode step of one block for M <= 16 tokens, each kernel cooperative and fused end to end: replaces the patched
+ * single-token MoE forward (engine.py:371-386: fused_ops.moe_route followed by fused_moe.fused_moe_decode),
+ * including the RMSNorm before it (engine.py:229) and the decoder layer's residual. One launch, except that the
+ * one-token kernel runs once per token for bf16 M = 2 and int8 M >= 2 (the block is per-token work, and there
+ * that is faster). x [M, H] bf16 contiguous, out [M, H] bf16.
  * Optional router outputs (each may be NULL): logits_out [M, E] f32, ids_out [M, top_k + n_shared]
  * (i32/i64), wts_out [M, top_k + n_shared] f32 -- the aux the reference block returns.
  * workspace: mv_block_decode_workspace_bytes(M, top_k + n_shared, I, E) bytes, zero-initialised. */
