@@ -176,6 +176,28 @@ def test_block_decode_int8(cuda, int8_params, M):
     no_device_errors()
 
 
+@pytest.mark.parametrize("int8,M", [(False, 2), (True, 2), (True, 5)])
+def test_block_decode_per_token_launches_match_single_tokens(cuda, base_params, int8_params, int8, M):
+    """bf16 M = 2 and int8 M >= 2 run the one-token kernel once per token: the rows, ids, weights and logits of
+    one M-token call are bitwise those of M one-token calls."""
+    from mingmoe.block import MoeBlock
+    blk = MoeBlock.from_params(int8_params if int8 else base_params)
+    x = O.make_tokens(M, seed=11).to(cuda)
+    ids = torch.empty(M, 8, dtype=torch.long, device=cuda)
+    wts = torch.empty(M, 8, device=cuda)
+    logits = torch.empty(M, 64, device=cuda)
+    y = blk.decode(x, logits=logits, ids=ids, wts=wts).clone()
+    for t in range(M):
+        ids1 = torch.empty(1, 8, dtype=torch.long, device=cuda)
+        wts1 = torch.empty(1, 8, device=cuda)
+        logits1 = torch.empty(1, 64, device=cuda)
+        y1 = blk.decode(x[t:t + 1].contiguous(), logits=logits1, ids=ids1, wts=wts1)
+        assert torch.equal(y1, y[t:t + 1])
+        assert torch.equal(ids1, ids[t:t + 1]) and torch.equal(wts1, wts[t:t + 1])
+        assert torch.equal(logits1, logits[t:t + 1])
+    no_device_errors()
+
+
 def test_block_decode_sigmoid_group_reference_model(cuda):
     """ming-voice's own router (sigmoid + bias, 8 groups keep 4, top-8, x2.5) with its shared expert in slot E."""
     from mingmoe.block import MoeBlock
